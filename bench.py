@@ -1,0 +1,380 @@
+"""Benchmark: W4A16 MoE-layer tokens/s at the LLaDA-MoE-7B-A1B shape on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one MoE layer forward (router + align + permute + W4A16 GEMM1 with
+SiLU + GEMM2 with routed weight + combine) over T=256 tokens (32 masked
+positions x batch 8, ~32 tokens/expert), E=64, H=2048, I=1024, top-8,
+INT4 group 128.  Synthetic seeded data: weights N(0,0.02)
+bf16 quantized by this package's pack kernel, x ~ N(0,1) bf16, router N(0,0.02).
+Steps rotate over 4 distinct layer weight sets (855 MB > the 126 MB L2), so no
+step reads weights left in L2 by the previous one.
+
+At N > 1 the layer runs expert-parallel (experts sharded contiguously, NCCL
+all-to-all dispatch/combine), T=256 tokens per rank (weak scaling).
+
+``--impl reference`` times the reference's CPU path (the numpy port of
+dequantize_tensor + the routed dequant-then-matmul, oracle/moe.py) on the host
+cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+E, H, I, TOPK, BITS, GROUP = 64, 2048, 1024, 8, 4, 128
+T_PER_RANK = 256
+N_LAYERS = 4
+METRIC = "W4A16 MoE-layer tokens/s (LLaDA-MoE-7B-A1B layer, T=256, top-8)"
+UNIT = "tokens/s"
+
+
+def layer_bytes(T: int, k: int, experts_hit: int) -> int:
+    """Algorithmic HBM bytes of one layer call: packed w1/w2 + fp32 scales of every expert
+    hit, x in, out written, router weights, routing ids + weights."""
+    per_expert = (2 * I * H // 2) + (2 * I * H // GROUP) * 4 + (H * I // 2) + (H * I // GROUP) * 4
+    return experts_hit * per_expert + 2 * T * H * 2 + E * H * 2 + T * k * 8
+
+
+def gemm1_bytes(n_rows: int, experts_hit: int) -> int:
+    """Bytes one GEMM1 launch must move: packed w1 + scales of the experts hit, the permuted
+    activation rows in, the bf16 SiLU(gate)*up rows out."""
+    return experts_hit * ((2 * I * H // 2) + (2 * I * H // GROUP) * 4) + n_rows * H * 2 + n_rows * I * 2
+
+
+def read_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def read_traffic(name: str):
+    """Per-launch DRAM bytes of the dominant kernel from its committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", name)
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.rows.append([c.strip() for c in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            for name, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(self.rows)}
+
+
+def cpu_reference(sample_layers: int = 1, threads=None):
+    """Time the reference CPU path (numpy port) on a bounded sample: ``sample_layers`` C3 layer
+    calls, each dequantizing every expert (what the PACKED property does) then the routed
+    dequant-then-matmul.  Returns (tokens/s, cores, seconds)."""
+    import numpy as np
+    import torch
+    from threadpoolctl import threadpool_limits
+
+    from oracle import moe as M
+    from oracle import symmetric as S
+
+    cores = threads or os.cpu_count()
+    g = torch.Generator().manual_seed(0)
+    w1 = (torch.randn(E, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
+    w2 = (torch.randn(E, H, I, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
+    q1, s1, *_ = S.quantize_tensor(w1, bits=BITS, group_size=GROUP)
+    q2, s2, *_ = S.quantize_tensor(w2, bits=BITS, group_size=GROUP)
+    del w1, w2
+    gate_w = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
+    x = torch.randn(T_PER_RANK, H, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).float().numpy()
+    with threadpool_limits(limits=cores):
+        t0 = time.perf_counter()
+        for _ in range(sample_layers):
+            M.moe_layer(x, gate_w, q1, s1, q2, s2, TOPK, BITS)
+        dt = time.perf_counter() - t0
+    return sample_layers * T_PER_RANK / dt, cores, dt
+
+
+def run_reference(args, rank: int):
+    if rank != 0:
+        return
+    vals = []
+    for _ in range(args.warmup):
+        cpu_reference(1)
+    for _ in range(args.steps):
+        v, cores, dt = cpu_reference(1)
+        vals.append(v)
+    value = statistics.median(vals)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": T_PER_RANK / value * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, bf16 activations, fp32 accumulate",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) tokens)", "impl": "reference",
+        "config": {"workload": "C3 LLaDA-MoE-7B-A1B layer: E=64 H=2048 I=1024 top-8 W4A16 g128, "
+                               "T=256 tokens per call", "tokens_per_step": T_PER_RANK},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": "one C3 layer call per step (numpy port of the reference's "
+                                   "PACKED dequantize + routed dequant-then-matmul)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def make_layers(device, n_layers: int, E_local: int, e0: int):
+    """Quantize ``n_layers`` seeded layer weight sets on the GPU with this package's pack kernel."""
+    import torch
+    from llada_quant_b200 import symmetric as G
+    from llada_quant_b200.moe import PackedExperts
+
+    layers = []
+    for l in range(n_layers):
+        g = torch.Generator(device=device).manual_seed(1000 + l)
+        packs = []
+        for shape in ((E, 2 * I, H), (E, H, I)):
+            w = (torch.randn(*shape, generator=g, device=device) * 0.02).to(torch.bfloat16)[e0:e0 + E_local]
+            r = G.quantize_tensor(w.contiguous(), bits=BITS, group_size=GROUP)
+            packs.append(r)
+            del w
+        layers.append(PackedExperts(packs[0].q, packs[0].scale, packs[1].q, packs[1].scale, BITS, GROUP))
+    g = torch.Generator(device=device).manual_seed(1)
+    gate_w = (torch.randn(E, H, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    return layers, gate_w
+
+
+def run_ours(args, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+
+    from llada_quant_b200 import ops
+    from llada_quant_b200.fused_moe import IMPL
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    impl = IMPL[args.gemm]
+    if world > 1:
+        from llada_quant_b200 import ep
+        E_local = E // world
+        layers, gate_w = make_layers(device, N_LAYERS, E_local, rank * E_local)
+    else:
+        E_local = E
+        layers, gate_w = make_layers(device, N_LAYERS, E, 0)
+    g = torch.Generator(device=device).manual_seed(2 + rank)
+    xs = [torch.randn(T_PER_RANK, H, generator=g, device=device).to(torch.bfloat16) for _ in range(N_LAYERS)]
+    bias = None
+
+    def step(i):
+        layer = layers[i % N_LAYERS]
+        x = xs[i % N_LAYERS]
+        if world > 1:
+            return ep.ep_moe_layer(x, gate_w, layer, TOPK, rank, world, bias=bias, impl=impl)
+        tw, ids, _ = ops.route(x, gate_w, TOPK, bias, False)
+        return ops.fused_moe_packed(x, layer.qw1, layer.sw1, layer.qw2, layer.sw2, tw, ids, BITS, impl)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- warm-up + timed device region -------------------------------------------
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        start.record()
+        for i in range(args.steps):
+            step(i)
+        end.record()
+        torch.cuda.synchronize()
+    barrier()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    tokens_per_step = T_PER_RANK * world
+    value = tokens_per_step / (ms_per_step / 1e3)
+
+    # ---- end to end through the public API with pinned host buffers ---------------
+    from llada_quant_b200.fused_moe import moe_layer
+    x_host = [x.cpu().pin_memory() for x in xs]
+    out_host = torch.empty(T_PER_RANK, H, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step(i):
+        x = x_host[i % N_LAYERS].to(device, non_blocking=True)
+        if world > 1:
+            from llada_quant_b200 import ep
+            out = ep.ep_moe_layer(x, gate_w, layers[i % N_LAYERS], TOPK, rank, world, impl=impl)
+        else:
+            out = moe_layer(x, gate_w, layers[i % N_LAYERS], TOPK, impl=args.gemm)
+        out_host.copy_(out, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    barrier()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for i in range(args.steps):
+        e2e_step(i)
+    e2.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = s2.elapsed_time(e2)
+    if world > 1:
+        t = torch.tensor([ms_e2e], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    e2e_value = tokens_per_step / (ms_e2e / args.steps / 1e3)
+
+    # ---- dominant kernel (GEMM1) timed alone with CUDA events ----------------------
+    kernel = None
+    if world == 1:
+        preps = []
+        for l in range(N_LAYERS):
+            tw, ids, _ = ops.route(xs[l], gate_w, TOPK, None, False)
+            offsets, slots = ops.moe_align(ids, E)
+            xsrt = ops.moe_permute(xs[l], slots, TOPK)
+            hit = int((offsets[1:] - offsets[:-1] > 0).sum().item())
+            preps.append((xsrt, offsets, hit))
+        for l in range(N_LAYERS):
+            ops.moe_gemm1(preps[l][0], preps[l][1], layers[l].qw1, layers[l].sw1, BITS, impl)
+        torch.cuda.synchronize()
+        reps = max(args.steps, 8)
+        ks, ke = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ks.record()
+        for i in range(reps):
+            l = i % N_LAYERS
+            ops.moe_gemm1(preps[l][0], preps[l][1], layers[l].qw1, layers[l].sw1, BITS, impl)
+        ke.record()
+        torch.cuda.synchronize()
+        k_ms = ks.elapsed_time(ke) / reps
+        n_rows = T_PER_RANK * TOPK
+        hit = statistics.mean(p[2] for p in preps)
+        algo = gemm1_bytes(n_rows, int(round(hit)))
+        peak, peak_kind = read_peaks()
+        achieved = algo / (k_ms / 1e3) / 1e9
+        kernel = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                  "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                  "traffic": read_traffic(f"gemm1_{args.gemm}_c3.txt"), "kernel": "moe GEMM1 (W4A16, SiLU epilogue)",
+                  "algorithmic_bytes": algo, "launch_ms": round(k_ms, 5)}
+        layer_algo = layer_bytes(T_PER_RANK, TOPK, int(round(hit)))
+        layer_gbs = layer_algo / (ms_per_step / 1e3) / 1e9
+        kernel["layer"] = {"algorithmic_bytes": layer_algo, "achieved": round(layer_gbs, 1),
+                           "frac": round(layer_gbs / peak, 4)}
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            v, cores, dt = cpu_reference(1)
+            cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+                   "sample": f"one C3 layer call (256 tokens) of the numpy port of the reference CPU path, {dt:.1f} s"}
+        launches_per_step = 8 if world == 1 else None
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, bf16 activations, fp32 accumulate",
+            "data": "synthetic (seeded N(0,0.02) weights quantized on device, N(0,1) tokens)",
+            "config": {"workload": "C3 LLaDA-MoE-7B-A1B layer: E=64 H=2048 I=1024 top-8 W4A16 g128",
+                       "tokens_per_rank": T_PER_RANK, "gemm": args.gemm,
+                       "parallelism": "ep%d" % world if world > 1 else "single",
+                       "l2": "inputs larger than L2: 4 rotated layer weight sets (4 x 214 MB)"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T_PER_RANK * H * 2,
+                    "d2h_bytes_per_step": T_PER_RANK * H * 2},
+            "gpu_launches": (launches_per_step * args.steps) if launches_per_step else None,
+            "roofline": kernel,
+            "cpu_baseline": cpu,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--gemm", choices=["auto", "tcgen05", "simt"], default="auto")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,192 @@
+/*
+ * llada_quant.h -- C ABI of libllada_quant_cuda.so, the B200 (sm_100a) kernels
+ * of LLaDA_Quant's quantized MoE expert path.
+ *
+ * Conventions
+ *   - Plain pointers to DEVICE memory, sizes in elements, a cudaStream_t passed
+ *     as void* (NULL = legacy default stream).  Every call is stream-ordered and
+ *     asynchronous; none synchronizes the host.
+ *   - The caller allocates every input, output and workspace
+ *     (llq_moe_workspace_size says how much); the library never frees caller
+ *     memory.
+ *   - Return value: LLQ_OK (0) or an error code; llq_last_error() gives the
+ *     message of the last failing call on the calling thread.  No C++ exception
+ *     crosses this boundary.
+ *   - Weights use the frozen LLaDA_Quant packed layout: q int8 [rows, K/2]
+ *     (INT4, element 2i in the low nibble, two's complement) or [rows, K]
+ *     (INT8); scale float32 [rows, K/group] (one scale per row when the group
+ *     does not divide K, group == -1 in LLaDA_Quant's terms).
+ *
+ * Each entry point names the reference interface it replaces, by path within
+ * the LLaDA_Quant project.
+ */
+#ifndef LLADA_QUANT_H
+#define LLADA_QUANT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum llq_status {
+  LLQ_OK = 0,
+  LLQ_EINVAL = 1,       /* bad shape, pointer, alignment or argument */
+  LLQ_EUNSUPPORTED = 2, /* valid but not implemented (bits, group, dtype) */
+  LLQ_ECUDA = 3,        /* a CUDA launch or runtime call failed */
+  LLQ_ETIMEOUT = 4,     /* a bounded device-side wait gave up */
+  LLQ_ENOSPACE = 5      /* workspace too small */
+};
+
+enum llq_dtype { LLQ_F32 = 0, LLQ_F16 = 1, LLQ_BF16 = 2 };
+
+enum llq_scale_search { LLQ_SEARCH_AMAX = 0, LLQ_SEARCH_MSE = 1 };
+
+enum llq_gemm_impl { LLQ_GEMM_AUTO = 0, LLQ_GEMM_TCGEN05 = 1, LLQ_GEMM_SIMT = 2 };
+
+/* Library version (major*10000 + minor*100 + patch). */
+int llq_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* llq_last_error(void);
+
+/* ------------------------------------------------------------------------ */
+/* Quantize and pack.                                                        */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Symmetric groupwise quantization of w [rows, K] along K, bit-exact with
+ * quantize_tensor() (src/LLaDA_Quant/algorithms/symmetric.py:207-269) and,
+ * for search == LLQ_SEARCH_MSE, search_group_scale() (:122-204) with the
+ * given grid and max_shrink.  group_size == -1, or a group that does not
+ * divide K, gives one scale per row (the fallback of _as_groups, :85-90).
+ * scale_round rounds the chosen scale to that dtype before it is used and
+ * stored (QuantConfig.scale_dtype): LLQ_F32 = keep.
+ * pack != 0 with bits == 4 writes two values per byte (pack_int4, :296-313);
+ * otherwise q holds one int8 per value.
+ */
+int llq_quantize_pack(const void* w, int w_dtype, int64_t rows, int64_t K, int bits,
+                      int group_size, int search, int grid, double max_shrink,
+                      int scale_round, int pack, int8_t* q, float* scale, void* stream);
+
+/*
+ * Per-group squared error of each MSE candidate (diagnostics for the
+ * reduction-order analysis of search_group_scale, symmetric.py:188-202):
+ * errors [rows * groups, grid] float32.
+ */
+int llq_search_errors(const void* w, int w_dtype, int64_t rows, int64_t K, int bits,
+                      int group_size, int grid, double max_shrink, float* errors,
+                      void* stream);
+
+/*
+ * w ~= q * scale, fp32 arithmetic then one rounding to out_dtype
+ * (dequantize_tensor, symmetric.py:272-293).  packed != 0: INT4 storage.
+ */
+int llq_dequantize(const int8_t* q, const float* scale, int64_t rows, int64_t K, int bits,
+                   int group_size, int packed, void* out, int out_dtype, void* stream);
+
+/* pack_int4 / unpack_int4 (symmetric.py:296-346); n = number of int4 values. */
+int llq_pack_int4(const int8_t* values, int64_t n, int8_t* packed, int32_t* range_error,
+                  void* stream);
+int llq_unpack_int4(const int8_t* packed, int64_t n, int8_t* values, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Routing.                                                                  */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Router of the external TritonFusedMoEBlock as RouterCapture recomputes it
+ * (src/LLaDA_Quant/trajectory/llada.py:225-234): logits = gate(x) in bf16
+ * (fp32 accumulation, one rounding), p = softmax(logits + bias) in fp32,
+ * top-k (larger value first, ties to the smaller expert id).  x bf16 [T, H],
+ * gate_w bf16 [E, H], bias float32 [E] or NULL, logits bf16 [T, E] or NULL.
+ * renormalize != 0 divides the k weights by their sum.  E <= 256, k <= E.
+ */
+int llq_route(const void* x, const void* gate_w, int64_t T, int H, int E, int k,
+              const float* bias, int renormalize, void* logits, float* topk_w,
+              int32_t* topk_ids, void* stream);
+
+/* Softmax + top-k from given logits (bf16 or f32) [T, E]. */
+int llq_route_topk(const void* logits, int logits_dtype, int64_t T, int E, int k,
+                   const float* bias, int renormalize, float* topk_w, int32_t* topk_ids,
+                   void* stream);
+
+/*
+ * moe_align_block_size of the external fused_moe (described in
+ * INFERENCE_REPO_CHANGES.md:274-278): group the T*k (token, slot) entries by
+ * expert, stable in entry order.  expert_offsets int32 [E+1]; sorted_slots
+ * int32 [T*k] holds token*k + slot.  workspace >= llq_align_workspace_size.
+ */
+size_t llq_align_workspace_size(int64_t T, int k, int E);
+int llq_moe_align(const int32_t* topk_ids, int64_t T, int k, int E, int32_t* expert_offsets,
+                  int32_t* sorted_slots, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Permute: x_sorted[p] = x[sorted_slots[p] / k], bf16 rows of H. */
+int llq_moe_permute(const void* x, int64_t T, int H, int k, const int32_t* sorted_slots,
+                    void* x_sorted, void* stream);
+
+/* Unpermute/combine: out[t] = bf16(sum_j y_slots[t*k + j]) in fp32, slot order. */
+int llq_moe_combine(const void* y_slots, int64_t T, int k, int H, void* out, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Grouped W4A16 / W8A16 expert GEMMs over the packed buffers.                */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * GEMM1 of the external fused_moe with the SiLU epilogue
+ * (INFERENCE_REPO_CHANGES.md:37-59, 296-309) reading PACKED w1 directly
+ * (replaces runtime/moe.py:199-216 + the bf16 fused_moe_kernel):
+ * for every sorted row p of expert e,
+ *   gate = bf16(x_sorted[p] . W1[e, n]),  up = bf16(x_sorted[p] . W1[e, I+n]),
+ *   h_sorted[p, n] = bf16(bf16(silu(gate)) * up)
+ * with W1 = bf16(q * scale) exactly as dequantize_tensor.
+ * qw1 int8 [E, 2I, H/2 or H], sw1 float32 [E, 2I, H/group].
+ */
+int llq_moe_gemm1(const void* x_sorted, const int32_t* expert_offsets, int64_t n_rows, int E,
+                  int H, int I, const int8_t* qw1, const float* sw1, int bits, int group_size,
+                  void* h_sorted, int impl, void* stream);
+
+/*
+ * GEMM2 with MUL_ROUTED_WEIGHT (INFERENCE_REPO_CHANGES.md:259-265), scattered
+ * back to (token, slot) order: y_slots[sorted_slots[p]] =
+ * bf16((h_sorted[p] . W2[e]) * topk_w[sorted_slots[p]]).
+ * qw2 int8 [E, H, I/2 or I], sw2 float32 [E, H, I/group].
+ */
+int llq_moe_gemm2(const void* h_sorted, const int32_t* expert_offsets,
+                  const int32_t* sorted_slots, const float* topk_w, int64_t n_rows, int E,
+                  int H, int I, const int8_t* qw2, const float* sw2, int bits, int group_size,
+                  void* y_slots, int impl, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Whole layer.                                                              */
+/* ------------------------------------------------------------------------ */
+
+/* Workspace bytes for llq_fused_moe_packed. */
+size_t llq_moe_workspace_size(int64_t T, int k, int E, int H, int I);
+
+/*
+ * fused_moe(hidden_states, w1, w2, gating_output, topk_ids) on PACKED weights
+ * (signature: INFERENCE_REPO_CHANGES.md:109-111; PACKED property:
+ * runtime/moe.py:199-216): align -> permute -> GEMM1 -> GEMM2 -> combine.
+ * x bf16 [T, H], topk_w float32 [T, k], topk_ids int32 [T, k], out bf16 [T, H].
+ */
+int llq_fused_moe_packed(const void* x, const int8_t* qw1, const float* sw1, const int8_t* qw2,
+                         const float* sw2, const float* topk_w, const int32_t* topk_ids,
+                         int64_t T, int E, int H, int I, int k, int bits, int group_size,
+                         void* out, void* workspace, size_t workspace_bytes, int impl,
+                         void* stream);
+
+/*
+ * Device error word written by bounded waits inside the tcgen05 kernels
+ * (0 = none).  Reading it synchronizes the device.  llq_clear_device_error
+ * resets it.
+ */
+int llq_device_error(int32_t* code);
+int llq_clear_device_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LLADA_QUANT_H */

@@ -1,0 +1,230 @@
+// extern "C" boundary of libllada_quant_cuda.so (declared in include/llada_quant.h).
+#include <cstdarg>
+#include <cstring>
+
+#include "llq_common.cuh"
+
+namespace llq {
+
+__device__ int32_t g_device_error = 0;
+
+namespace {
+thread_local char t_error[512] = {0};
+}
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_error, sizeof(t_error), fmt, ap);
+  va_end(ap);
+}
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_error, sizeof(t_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+const char* last_error() { return t_error; }
+
+// implemented in the kernel files
+int quantize_impl(const void*, int, int64_t, int64_t, int, int, int, int, double, int, int, int8_t*,
+                  float*, float*, cudaStream_t);
+int dequantize_impl(const int8_t*, const float*, int64_t, int64_t, int, int, int, void*, int,
+                    cudaStream_t);
+int pack_int4_impl(const int8_t*, int64_t, int8_t*, int32_t*, cudaStream_t);
+int unpack_int4_impl(const int8_t*, int64_t, int8_t*, cudaStream_t);
+int route_impl(const void*, const void*, int64_t, int, int, int, const float*, int, void*, float*,
+               int32_t*, cudaStream_t);
+int route_topk_impl(const void*, int, int64_t, int, int, const float*, int, float*, int32_t*,
+                    cudaStream_t);
+size_t align_workspace_size(int64_t, int, int);
+int align_impl(const int32_t*, int64_t, int, int, int32_t*, int32_t*, void*, size_t, cudaStream_t);
+int permute_impl(const void*, int64_t, int, int, const int32_t*, void*, cudaStream_t);
+int combine_impl(const void*, int64_t, int, int, void*, cudaStream_t);
+int gemm1_simt(const void*, const int32_t*, int, int, int, const int8_t*, const float*, int, int,
+               void*, cudaStream_t);
+int gemm2_simt(const void*, const int32_t*, const int32_t*, const float*, int, int, int,
+               const int8_t*, const float*, int, int, void*, cudaStream_t);
+int gemm1_tc(const void*, const int32_t*, int64_t, int, int, int, const int8_t*, const float*, int,
+             int, void*, cudaStream_t);
+int gemm2_tc(const void*, const int32_t*, const int32_t*, const float*, int64_t, int, int, int,
+             const int8_t*, const float*, int, int, void*, cudaStream_t);
+bool tc_supported(int E, int N_out, int K, int bits, int group_size, bool gemm1);
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+struct MoeWorkspace {
+  int32_t* offsets;
+  int32_t* sorted_slots;
+  void* align_ws;
+  size_t align_bytes;
+  void* x_sorted;
+  void* h_sorted;
+  void* y_slots;
+  size_t total;
+};
+
+MoeWorkspace carve(void* base, int64_t T, int k, int E, int H, int I) {
+  MoeWorkspace w{};
+  const int64_t n = T * k;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes, 256);
+    return static_cast<char*>(base) + o;
+  };
+  w.offsets = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * (E + 1)));
+  w.sorted_slots = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * (n > 0 ? n : 1)));
+  w.align_bytes = align_workspace_size(T, k, E);
+  w.align_ws = take(w.align_bytes);
+  w.x_sorted = take(static_cast<size_t>(n) * H * 2 + 4096);
+  w.h_sorted = take(static_cast<size_t>(n) * I * 2 + 4096);
+  w.y_slots = take(static_cast<size_t>(n) * H * 2 + 4096);
+  w.total = off;
+  return w;
+}
+
+int pick_impl(int impl, int E, int N_out, int K, int bits, int group_size, bool gemm1) {
+  if (impl == LLQ_GEMM_SIMT) return LLQ_GEMM_SIMT;
+  const bool tc = tc_supported(E, N_out, K, bits, group_size, gemm1);
+  if (impl == LLQ_GEMM_TCGEN05) return tc ? LLQ_GEMM_TCGEN05 : -1;
+  return tc ? LLQ_GEMM_TCGEN05 : LLQ_GEMM_SIMT;
+}
+
+}  // namespace llq
+
+using namespace llq;
+
+extern "C" {
+
+int llq_version(void) { return 100; }
+
+const char* llq_last_error(void) { return llq::last_error(); }
+
+int llq_quantize_pack(const void* w, int w_dtype, int64_t rows, int64_t K, int bits, int group_size,
+                      int search, int grid, double max_shrink, int scale_round, int pack, int8_t* q,
+                      float* scale, void* stream) {
+  return quantize_impl(w, w_dtype, rows, K, bits, group_size, search, grid, max_shrink, scale_round,
+                       pack, q, scale, nullptr, as_stream(stream));
+}
+
+int llq_search_errors(const void* w, int w_dtype, int64_t rows, int64_t K, int bits, int group_size,
+                      int grid, double max_shrink, float* errors, void* stream) {
+  if (errors == nullptr) return fail(LLQ_EINVAL, "null errors pointer");
+  return quantize_impl(w, w_dtype, rows, K, bits, group_size, LLQ_SEARCH_MSE, grid, max_shrink,
+                       LLQ_F32, 0, nullptr, nullptr, errors, as_stream(stream));
+}
+
+int llq_dequantize(const int8_t* q, const float* scale, int64_t rows, int64_t K, int bits,
+                   int group_size, int packed, void* out, int out_dtype, void* stream) {
+  return dequantize_impl(q, scale, rows, K, bits, group_size, packed, out, out_dtype, as_stream(stream));
+}
+
+int llq_pack_int4(const int8_t* values, int64_t n, int8_t* packed, int32_t* range_error, void* stream) {
+  if (range_error == nullptr) return fail(LLQ_EINVAL, "range_error must point to a device int32");
+  return pack_int4_impl(values, n, packed, range_error, as_stream(stream));
+}
+
+int llq_unpack_int4(const int8_t* packed, int64_t n, int8_t* values, void* stream) {
+  return unpack_int4_impl(packed, n, values, as_stream(stream));
+}
+
+int llq_route(const void* x, const void* gate_w, int64_t T, int H, int E, int k, const float* bias,
+              int renormalize, void* logits, float* topk_w, int32_t* topk_ids, void* stream) {
+  return route_impl(x, gate_w, T, H, E, k, bias, renormalize, logits, topk_w, topk_ids, as_stream(stream));
+}
+
+int llq_route_topk(const void* logits, int logits_dtype, int64_t T, int E, int k, const float* bias,
+                   int renormalize, float* topk_w, int32_t* topk_ids, void* stream) {
+  return route_topk_impl(logits, logits_dtype, T, E, k, bias, renormalize, topk_w, topk_ids,
+                         as_stream(stream));
+}
+
+size_t llq_align_workspace_size(int64_t T, int k, int E) { return align_workspace_size(T, k, E); }
+
+int llq_moe_align(const int32_t* topk_ids, int64_t T, int k, int E, int32_t* expert_offsets,
+                  int32_t* sorted_slots, void* workspace, size_t workspace_bytes, void* stream) {
+  return align_impl(topk_ids, T, k, E, expert_offsets, sorted_slots, workspace, workspace_bytes,
+                    as_stream(stream));
+}
+
+int llq_moe_permute(const void* x, int64_t T, int H, int k, const int32_t* sorted_slots, void* x_sorted,
+                    void* stream) {
+  return permute_impl(x, T, H, k, sorted_slots, x_sorted, as_stream(stream));
+}
+
+int llq_moe_combine(const void* y_slots, int64_t T, int k, int H, void* out, void* stream) {
+  return combine_impl(y_slots, T, k, H, out, as_stream(stream));
+}
+
+int llq_moe_gemm1(const void* x_sorted, const int32_t* expert_offsets, int64_t n_rows, int E, int H,
+                  int I, const int8_t* qw1, const float* sw1, int bits, int group_size,
+                  void* h_sorted, int impl, void* stream) {
+  const int which = pick_impl(impl, E, I, H, bits, group_size, true);
+  if (which < 0) return fail(LLQ_EUNSUPPORTED, "tcgen05 GEMM1 does not cover this shape");
+  if (which == LLQ_GEMM_TCGEN05)
+    return gemm1_tc(x_sorted, expert_offsets, n_rows, E, H, I, qw1, sw1, bits, group_size,
+                    h_sorted, as_stream(stream));
+  return gemm1_simt(x_sorted, expert_offsets, E, H, I, qw1, sw1, bits, group_size, h_sorted,
+                    as_stream(stream));
+}
+
+int llq_moe_gemm2(const void* h_sorted, const int32_t* expert_offsets, const int32_t* sorted_slots,
+                  const float* topk_w, int64_t n_rows, int E, int H, int I, const int8_t* qw2,
+                  const float* sw2, int bits, int group_size, void* y_slots, int impl, void* stream) {
+  const int which = pick_impl(impl, E, H, I, bits, group_size, false);
+  if (which < 0) return fail(LLQ_EUNSUPPORTED, "tcgen05 GEMM2 does not cover this shape");
+  if (which == LLQ_GEMM_TCGEN05)
+    return gemm2_tc(h_sorted, expert_offsets, sorted_slots, topk_w, n_rows, E, H, I, qw2, sw2,
+                    bits, group_size, y_slots, as_stream(stream));
+  return gemm2_simt(h_sorted, expert_offsets, sorted_slots, topk_w, E, H, I, qw2, sw2, bits,
+                    group_size, y_slots, as_stream(stream));
+}
+
+size_t llq_moe_workspace_size(int64_t T, int k, int E, int H, int I) {
+  return carve(nullptr, T, k, E, H, I).total;
+}
+
+int llq_fused_moe_packed(const void* x, const int8_t* qw1, const float* sw1, const int8_t* qw2,
+                         const float* sw2, const float* topk_w, const int32_t* topk_ids, int64_t T,
+                         int E, int H, int I, int k, int bits, int group_size, void* out,
+                         void* workspace, size_t workspace_bytes, int impl, void* stream) {
+  if (T < 0 || E < 1 || H < 1 || I < 1 || k < 1 || k > E)
+    return fail(LLQ_EINVAL, "bad shape T=%lld E=%d H=%d I=%d k=%d", (long long)T, E, H, I, k);
+  if (T == 0) return LLQ_OK;
+  MoeWorkspace ws = carve(workspace, T, k, E, H, I);
+  if (workspace == nullptr || workspace_bytes < ws.total)
+    return fail(LLQ_ENOSPACE, "workspace needs %zu bytes, got %zu", ws.total, workspace_bytes);
+  cudaStream_t st = as_stream(stream);
+  const int64_t n = T * k;
+  int rc = align_impl(topk_ids, T, k, E, ws.offsets, ws.sorted_slots, ws.align_ws, ws.align_bytes, st);
+  if (rc) return rc;
+  rc = permute_impl(x, T, H, k, ws.sorted_slots, ws.x_sorted, st);
+  if (rc) return rc;
+  rc = llq_moe_gemm1(ws.x_sorted, ws.offsets, n, E, H, I, qw1, sw1, bits, group_size, ws.h_sorted,
+                     impl, stream);
+  if (rc) return rc;
+  rc = llq_moe_gemm2(ws.h_sorted, ws.offsets, ws.sorted_slots, topk_w, n, E, H, I, qw2, sw2, bits,
+                     group_size, ws.y_slots, impl, stream);
+  if (rc) return rc;
+  return combine_impl(ws.y_slots, T, k, H, out, st);
+}
+
+int llq_device_error(int32_t* code) {
+  if (code == nullptr) return fail(LLQ_EINVAL, "null code pointer");
+  cudaError_t e = cudaMemcpyFromSymbol(code, g_device_error, sizeof(int32_t));
+  if (e != cudaSuccess) return fail(LLQ_ECUDA, "reading the device error word: %s", cudaGetErrorString(e));
+  return LLQ_OK;
+}
+
+int llq_clear_device_error(void) {
+  const int32_t zero = 0;
+  cudaError_t e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int32_t));
+  if (e != cudaSuccess) return fail(LLQ_ECUDA, "clearing the device error word: %s", cudaGetErrorString(e));
+  return LLQ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,403 @@
+// Router (logits + softmax + top-k), expert alignment, permute and combine.
+//
+// Routing restates RouterCapture's recomputation of the external block's
+// router (src/LLaDA_Quant/trajectory/llada.py:225-234):
+//   logits = bf16(x . gate_w^T)   fp32 accumulation, one rounding
+//   p      = softmax(logits (+ bias), fp32)  = exp(l - max) * (1 / sum)
+//   top-k  larger p first; equal p -> smaller expert id (torch's CPU topk
+//          leaves that order unspecified)
+// Alignment groups the T*k (token, slot) entries by expert, stable in entry
+// order (the contract of the external moe_align_block_size,
+// INFERENCE_REPO_CHANGES.md:274-278).
+#include "llq_common.cuh"
+
+namespace llq {
+
+namespace {
+
+constexpr int kMaxExperts = 256;
+constexpr int kRouteTokens = 4;  // tokens per block in the fused router
+
+// softmax + top-k of one token held by one warp: value j of the lane is
+// expert lane + 32 j
+__device__ void warp_softmax_topk(float (&v)[kMaxExperts / 32], int E, int k, int renormalize,
+                                  float* __restrict__ topk_w, int32_t* __restrict__ topk_ids) {
+  const int lane = threadIdx.x & 31;
+  constexpr int J = kMaxExperts / 32;
+  float m = -__int_as_float(0x7f800000);
+#pragma unroll
+  for (int j = 0; j < J; ++j)
+    if (lane + 32 * j < E) m = fmaxf(m, v[j]);
+  m = warp_max(m);
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    if (lane + 32 * j < E) {
+      v[j] = expf(__fsub_rn(v[j], m));
+      s = __fadd_rn(s, v[j]);
+    }
+  }
+  s = warp_sum(s);
+  const float inv = __fdiv_rn(1.f, s);
+#pragma unroll
+  for (int j = 0; j < J; ++j) v[j] = (lane + 32 * j < E) ? __fmul_rn(v[j], inv) : -1.f;
+
+  float wsum = 0.f;
+  float chosen_w = 0.f;
+  int chosen_id = 0;
+  for (int r = 0; r < k; ++r) {
+    // lane-local best, then warp argmax with (value desc, id asc)
+    float bv = -2.f;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int id = lane + 32 * j;
+      if (id < E && (v[j] > bv || (v[j] == bv && id < bi))) {
+        bv = v[j];
+        bi = id;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    // remove the winner
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+      if (lane + 32 * j == bi) v[j] = -2.f;
+    if (lane == r) {
+      chosen_w = bv;
+      chosen_id = bi;
+    }
+    wsum = __fadd_rn(wsum, bv);
+  }
+  if (lane < k) {
+    topk_ids[lane] = chosen_id;
+    topk_w[lane] = renormalize ? __fdiv_rn(chosen_w, wsum) : chosen_w;
+  }
+}
+
+// logits + softmax + top-k for kRouteTokens tokens per block.
+__global__ void __launch_bounds__(256) route_kernel(const __nv_bfloat16* __restrict__ x,
+                                                    const __nv_bfloat16* __restrict__ gate_w,
+                                                    int64_t T, int H, int E, int k,
+                                                    const float* __restrict__ bias, int renormalize,
+                                                    __nv_bfloat16* __restrict__ logits_out,
+                                                    float* __restrict__ topk_w,
+                                                    int32_t* __restrict__ topk_ids) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);        // [kRouteTokens][H]
+  float* lg = reinterpret_cast<float*>(xs + kRouteTokens * static_cast<int64_t>(H));  // [kRouteTokens][E]
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kRouteTokens;
+  const int nt = static_cast<int>(T - t0 < kRouteTokens ? T - t0 : kRouteTokens);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // stage the token rows (16-byte vectors; H % 8 == 0 checked on the host)
+  const int vec_per_row = H / 8;
+  for (int i = threadIdx.x; i < kRouteTokens * vec_per_row; i += blockDim.x) {
+    const int t = i / vec_per_row, v = i - t * vec_per_row;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (t < nt) val = reinterpret_cast<const uint4*>(x + (t0 + t) * H)[v];
+    reinterpret_cast<uint4*>(xs + static_cast<int64_t>(t) * H)[v] = val;
+  }
+  __syncthreads();
+
+  for (int e = warp; e < E; e += blockDim.x / 32) {
+    float acc[kRouteTokens];
+#pragma unroll
+    for (int t = 0; t < kRouteTokens; ++t) acc[t] = 0.f;
+    const uint4* wrow = reinterpret_cast<const uint4*>(gate_w + static_cast<int64_t>(e) * H);
+    for (int v = lane; v < vec_per_row; v += 32) {
+      const uint4 wv = __ldg(wrow + v);
+      const __nv_bfloat16* wp = reinterpret_cast<const __nv_bfloat16*>(&wv);
+#pragma unroll
+      for (int t = 0; t < kRouteTokens; ++t) {
+        const uint4 xv = reinterpret_cast<const uint4*>(xs + static_cast<int64_t>(t) * H)[v];
+        const __nv_bfloat16* xp = reinterpret_cast<const __nv_bfloat16*>(&xv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          acc[t] = __fmaf_rn(__bfloat162float(xp[i]), __bfloat162float(wp[i]), acc[t]);
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < kRouteTokens; ++t) {
+      const float l = round_bf16(warp_sum(acc[t]));
+      if (lane == 0) lg[t * E + e] = l;
+    }
+  }
+  __syncthreads();
+
+  if (warp < nt) {
+    const int64_t t = t0 + warp;
+    float v[kMaxExperts / 32];
+#pragma unroll
+    for (int j = 0; j < kMaxExperts / 32; ++j) {
+      const int id = lane + 32 * j;
+      float l = 0.f;
+      if (id < E) {
+        l = lg[warp * E + id];
+        if (logits_out != nullptr) logits_out[t * E + id] = __float2bfloat16_rn(l);
+        if (bias != nullptr) l = __fadd_rn(l, bias[id]);
+      }
+      v[j] = l;
+    }
+    warp_softmax_topk(v, E, k, renormalize, topk_w + t * k, topk_ids + t * k);
+  }
+}
+
+template <typename L>
+__global__ void route_topk_kernel(const L* __restrict__ logits, int64_t T, int E, int k,
+                                  const float* __restrict__ bias, int renormalize,
+                                  float* __restrict__ topk_w, int32_t* __restrict__ topk_ids) {
+  const int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (t >= T) return;
+  const int lane = threadIdx.x & 31;
+  float v[kMaxExperts / 32];
+#pragma unroll
+  for (int j = 0; j < kMaxExperts / 32; ++j) {
+    const int id = lane + 32 * j;
+    float l = 0.f;
+    if (id < E) {
+      l = to_f32<L>(logits[t * E + id]);
+      if (bias != nullptr) l = __fadd_rn(l, bias[id]);
+    }
+    v[j] = l;
+  }
+  warp_softmax_topk(v, E, k, renormalize, topk_w + t * k, topk_ids + t * k);
+}
+
+// ---------------------------------------------------------------------------
+// alignment: count -> scan -> stable scatter
+// ---------------------------------------------------------------------------
+constexpr int kAlignChunk = 2048;  // (token, slot) entries per block
+constexpr int kAlignThreads = 256;
+
+__global__ void __launch_bounds__(kAlignThreads) align_count_kernel(
+    const int32_t* __restrict__ ids, int64_t n, int E, int32_t* __restrict__ counts) {
+  __shared__ int32_t c[kMaxExperts];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) c[e] = 0;
+  __syncthreads();
+  const int64_t lo = static_cast<int64_t>(blockIdx.x) * kAlignChunk;
+  const int64_t hi = lo + kAlignChunk < n ? lo + kAlignChunk : n;
+  for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    const int e = ids[i];
+    if (e >= 0 && e < E) atomicAdd(&c[e], 1);
+    else atomicExch(&g_device_error, 2);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) counts[static_cast<int64_t>(blockIdx.x) * E + e] = c[e];
+}
+
+__global__ void __launch_bounds__(kMaxExperts) align_scan_kernel(int32_t* __restrict__ counts,
+                                                                 int nblk, int E,
+                                                                 int32_t* __restrict__ offsets) {
+  __shared__ int32_t tot[kMaxExperts + 1];
+  const int e = threadIdx.x;
+  int running = 0;
+  if (e < E) {
+    for (int b = 0; b < nblk; ++b) {
+      const int c = counts[static_cast<int64_t>(b) * E + e];
+      counts[static_cast<int64_t>(b) * E + e] = running;  // block base, relative to the expert
+      running += c;
+    }
+    tot[e] = running;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int i = 0; i < E; ++i) {
+      const int c = tot[i];
+      tot[i] = acc;
+      acc += c;
+    }
+    tot[E] = acc;
+  }
+  __syncthreads();
+  if (e < E) {
+    offsets[e] = tot[e];
+    for (int b = 0; b < nblk; ++b) counts[static_cast<int64_t>(b) * E + e] += tot[e];
+  }
+  if (e == 0) offsets[E] = tot[E];
+}
+
+__global__ void __launch_bounds__(kAlignThreads) align_scatter_kernel(
+    const int32_t* __restrict__ ids, int64_t n, int E, const int32_t* __restrict__ base,
+    int32_t* __restrict__ sorted_slots) {
+  __shared__ int32_t cursor[kMaxExperts];
+  __shared__ int32_t wcnt[kAlignThreads / 32][kMaxExperts];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cursor[e] = base[static_cast<int64_t>(blockIdx.x) * E + e];
+  for (int i = threadIdx.x; i < (kAlignThreads / 32) * kMaxExperts; i += blockDim.x)
+    (&wcnt[0][0])[i] = 0;
+  __syncthreads();
+  const int64_t lo = static_cast<int64_t>(blockIdx.x) * kAlignChunk;
+  const int64_t hi = lo + kAlignChunk < n ? lo + kAlignChunk : n;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int64_t r0 = lo; r0 < hi; r0 += kAlignThreads) {
+    const int64_t i = r0 + threadIdx.x;
+    int e = -1;
+    if (i < hi) {
+      e = ids[i];
+      if (e < 0 || e >= E) e = -1;
+    }
+    const unsigned same = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(same & lt_mask);
+    if (e >= 0 && rank == 0) wcnt[warp][e] = __popc(same);
+    __syncthreads();
+    int pos = 0;
+    if (e >= 0) {
+      pos = cursor[e] + rank;
+      for (int w = 0; w < warp; ++w) pos += wcnt[w][e];
+      sorted_slots[pos] = static_cast<int32_t>(i);
+    }
+    __syncthreads();
+    for (int ee = threadIdx.x; ee < E; ee += blockDim.x) {
+      int add = 0;
+      for (int w = 0; w < kAlignThreads / 32; ++w) {
+        add += wcnt[w][ee];
+        wcnt[w][ee] = 0;
+      }
+      cursor[ee] += add;
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void permute_kernel(const uint4* __restrict__ x, int64_t n_rows, int vec_per_row, int k,
+                               const int32_t* __restrict__ sorted_slots, uint4* __restrict__ xs) {
+  const int64_t total = n_rows * vec_per_row;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t p = i / vec_per_row;
+    const int v = static_cast<int>(i - p * vec_per_row);
+    const int64_t tok = sorted_slots[p] / k;
+    xs[i] = __ldg(x + tok * vec_per_row + v);
+  }
+}
+
+__global__ void combine_kernel(const uint4* __restrict__ y, int64_t T, int k, int vec_per_row,
+                               uint4* __restrict__ out) {
+  const int64_t total = T * vec_per_row;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / vec_per_row;
+    const int v = static_cast<int>(i - t * vec_per_row);
+    float acc[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const uint4 yv = __ldg(y + (t * k + j) * vec_per_row + v);
+      const __nv_bfloat16* yp = reinterpret_cast<const __nv_bfloat16*>(&yv);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] = __fadd_rn(acc[q], __bfloat162float(yp[q]));
+    }
+    uint4 o;
+    __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) op[q] = __float2bfloat16_rn(acc[q]);
+    out[i] = o;
+  }
+}
+
+inline unsigned grid_for(int64_t work, int threads) {
+  int64_t b = (work + threads - 1) / threads;
+  const int64_t cap = static_cast<int64_t>(num_sms()) * 32;
+  if (b > cap) b = cap;
+  if (b < 1) b = 1;
+  return static_cast<unsigned>(b);
+}
+
+}  // namespace
+
+int route_impl(const void* x, const void* gate_w, int64_t T, int H, int E, int k, const float* bias,
+               int renormalize, void* logits, float* topk_w, int32_t* topk_ids, cudaStream_t st) {
+  if (T <= 0) return LLQ_OK;
+  if (E < 1 || E > kMaxExperts) return fail(LLQ_EUNSUPPORTED, "num_experts must be in [1, 256], got %d", E);
+  if (k < 1 || k > E || k > 32) return fail(LLQ_EINVAL, "top_k must be in [1, min(E, 32)], got %d", k);
+  if (H % 8 != 0) return fail(LLQ_EUNSUPPORTED, "hidden size must be a multiple of 8, got %d", H);
+  const size_t smem = static_cast<size_t>(kRouteTokens) * H * 2 + static_cast<size_t>(kRouteTokens) * E * 4;
+  if (smem > 200 * 1024) return fail(LLQ_EUNSUPPORTED, "hidden size %d too large for the router", H);
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr_set = true;
+  }
+  const unsigned blocks = static_cast<unsigned>((T + kRouteTokens - 1) / kRouteTokens);
+  route_kernel<<<blocks, 256, smem, st>>>(static_cast<const __nv_bfloat16*>(x),
+                                          static_cast<const __nv_bfloat16*>(gate_w), T, H, E, k,
+                                          bias, renormalize, static_cast<__nv_bfloat16*>(logits),
+                                          topk_w, topk_ids);
+  return check_launch("route_kernel");
+}
+
+int route_topk_impl(const void* logits, int dtype, int64_t T, int E, int k, const float* bias,
+                    int renormalize, float* topk_w, int32_t* topk_ids, cudaStream_t st) {
+  if (T <= 0) return LLQ_OK;
+  if (E < 1 || E > kMaxExperts) return fail(LLQ_EUNSUPPORTED, "num_experts must be in [1, 256], got %d", E);
+  if (k < 1 || k > E || k > 32) return fail(LLQ_EINVAL, "top_k must be in [1, min(E, 32)], got %d", k);
+  const unsigned blocks = static_cast<unsigned>((T * 32 + 255) / 256);
+  if (dtype == LLQ_BF16)
+    route_topk_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(logits), T, E, k, bias, renormalize, topk_w, topk_ids);
+  else if (dtype == LLQ_F32)
+    route_topk_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(logits), T, E, k,
+                                                     bias, renormalize, topk_w, topk_ids);
+  else
+    return fail(LLQ_EUNSUPPORTED, "logits dtype %d", dtype);
+  return check_launch("route_topk_kernel");
+}
+
+size_t align_workspace_size(int64_t T, int k, int E) {
+  const int64_t n = T * k;
+  const int64_t nblk = (n + kAlignChunk - 1) / kAlignChunk;
+  return static_cast<size_t>((nblk < 1 ? 1 : nblk) * E * sizeof(int32_t) + 256);
+}
+
+int align_impl(const int32_t* ids, int64_t T, int k, int E, int32_t* offsets, int32_t* sorted_slots,
+               void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (E < 1 || E > kMaxExperts) return fail(LLQ_EUNSUPPORTED, "num_experts must be in [1, 256], got %d", E);
+  const int64_t n = T * k;
+  if (ws_bytes < align_workspace_size(T, k, E)) return fail(LLQ_ENOSPACE, "align workspace too small");
+  if (n == 0) {
+    cudaMemsetAsync(offsets, 0, sizeof(int32_t) * (E + 1), st);
+    return check_launch("align memset");
+  }
+  const int64_t nblk = (n + kAlignChunk - 1) / kAlignChunk;
+  if (nblk > 0x7fffffff) return fail(LLQ_EINVAL, "too many entries");
+  int32_t* counts = static_cast<int32_t*>(ws);
+  align_count_kernel<<<static_cast<unsigned>(nblk), kAlignThreads, 0, st>>>(ids, n, E, counts);
+  int rc = check_launch("align_count_kernel");
+  if (rc) return rc;
+  align_scan_kernel<<<1, kMaxExperts, 0, st>>>(counts, static_cast<int>(nblk), E, offsets);
+  rc = check_launch("align_scan_kernel");
+  if (rc) return rc;
+  align_scatter_kernel<<<static_cast<unsigned>(nblk), kAlignThreads, 0, st>>>(ids, n, E, counts, sorted_slots);
+  return check_launch("align_scatter_kernel");
+}
+
+int permute_impl(const void* x, int64_t T, int H, int k, const int32_t* sorted_slots, void* xs,
+                 cudaStream_t st) {
+  if (H % 8 != 0) return fail(LLQ_EUNSUPPORTED, "hidden size must be a multiple of 8");
+  const int64_t n = T * k;
+  if (n == 0) return LLQ_OK;
+  const int vpr = H / 8;
+  permute_kernel<<<grid_for(n * vpr, 256), 256, 0, st>>>(static_cast<const uint4*>(x), n, vpr, k,
+                                                         sorted_slots, static_cast<uint4*>(xs));
+  return check_launch("permute_kernel");
+}
+
+int combine_impl(const void* y, int64_t T, int k, int H, void* out, cudaStream_t st) {
+  if (H % 8 != 0) return fail(LLQ_EUNSUPPORTED, "hidden size must be a multiple of 8");
+  if (T == 0) return LLQ_OK;
+  const int vpr = H / 8;
+  combine_kernel<<<grid_for(T * vpr, 256), 256, 0, st>>>(static_cast<const uint4*>(y), T, k, vpr,
+                                                         static_cast<uint4*>(out));
+  return check_launch("combine_kernel");
+}
+
+}  // namespace llq

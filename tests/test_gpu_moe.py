@@ -1,0 +1,169 @@
+"""GPU parity of the routed W4A16/W8A16 expert FFN.
+
+Oracle: oracle/moe.py (bf16 weights exactly as the PACKED property returns
+them, fp32 accumulation, the external kernel's rounding order), pinned to the
+reference in tests/test_oracle_golden.py.
+
+Tolerance (stated): the kernels accumulate in fp32 in another order than the
+oracle, so a bf16 rounding of gate/up/h/y can land one ulp apart and carry
+forward.  Layer outputs: rel-L2 <= 3e-3 against the oracle (the bar of the
+reference's own kernel test, tests/unit/test_w8a16_kernel.py:59-66), and
+max-abs <= 2 bf16 ulps of the output's largest magnitude.  Per-GEMM outputs:
+rel-L2 <= 2e-3.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe as M
+from oracle import symmetric as S
+from tests._util import random_routing, synthetic_layer, synthetic_tokens, to_np
+
+pytestmark = pytest.mark.gpu
+
+IMPLS = ["simt", "tcgen05"]
+
+
+def _impl_or_skip(impl):
+    from llada_quant_b200 import _lib
+    if impl == "tcgen05":
+        return _lib.LLQ_GEMM_TCGEN05
+    return _lib.LLQ_GEMM_SIMT
+
+
+def _quantize(E, H, I, bits, search="amax", seed=0):
+    from llada_quant_b200 import symmetric as G
+    w1, w2 = synthetic_layer(E, H, I, seed=seed)
+    r1 = G.quantize_tensor(w1.cuda(), bits=bits, group_size=128, scale_search=search)
+    r2 = G.quantize_tensor(w2.cuda(), bits=bits, group_size=128, scale_search=search)
+    return r1, r2
+
+
+def _assert_layer_close(out, ref):
+    rel = M.rel_l2(out, ref)
+    mx = M.max_abs(out, ref)
+    bound = 2 * 2.0 ** -7 * max(np.abs(ref).max(), 1e-6)
+    assert rel <= 3e-3, rel
+    assert mx <= bound, (mx, bound)
+    return rel, mx
+
+
+def _run_layer(T, E, H, I, k, bits, impl, skew=None, search="amax", seed=0):
+    from llada_quant_b200 import ops
+    r1, r2 = _quantize(E, H, I, bits, search, seed)
+    x = synthetic_tokens(T, H)
+    tw, ids = random_routing(T, E, k, seed=seed + T, skew=skew)
+    try:
+        out = ops.fused_moe_packed(x.cuda(), r1.q, r1.scale, r2.q, r2.scale,
+                                   torch.from_numpy(tw).cuda(), torch.from_numpy(ids).cuda(), bits,
+                                   _impl_or_skip(impl))
+    except Exception as e:  # tcgen05 may decline a shape: that is a failure for supported shapes
+        raise
+    ref = M.fused_moe_packed(to_np(x), to_np(r1.q), to_np(r1.scale), to_np(r2.q), to_np(r2.scale),
+                             tw, ids, bits)
+    return to_np(out), ref
+
+
+@pytest.mark.parametrize("impl", IMPLS)
+@pytest.mark.parametrize("T,E,H,I,k,bits", [
+    (256, 16, 1024, 512, 2, 4),     # C1 layer
+    (1024, 16, 1024, 512, 2, 8),    # C2, W8A16
+    (256, 64, 2048, 1024, 8, 4),    # C3 layer
+    (33, 64, 2048, 1024, 8, 4),     # ragged, many empty experts
+    (1, 16, 1024, 512, 2, 4),       # single token
+    (7, 16, 1024, 512, 2, 8),
+])
+def test_fused_layer_matches_oracle(impl, T, E, H, I, k, bits):
+    out, ref = _run_layer(T, E, H, I, k, bits, impl)
+    _assert_layer_close(out, ref)
+
+
+@pytest.mark.parametrize("impl", IMPLS)
+def test_skewed_routing_one_hot_expert(impl):
+    """Zipf-skewed routing: one expert gets most tokens (> one token tile)."""
+    out, ref = _run_layer(600, 16, 1024, 512, 2, 4, impl, skew=3.0)
+    _assert_layer_close(out, ref)
+
+
+@pytest.mark.parametrize("impl", IMPLS)
+def test_mse_weights(impl):
+    out, ref = _run_layer(128, 16, 1024, 512, 2, 4, impl, search="mse")
+    _assert_layer_close(out, ref)
+
+
+@pytest.mark.parametrize("impl", IMPLS)
+@pytest.mark.parametrize("name", ["moe_i4_amax", "moe_i8_amax", "moe_i4_mse"])
+def test_layer_vs_reference_golden(golden, impl, name):
+    """Golden layer outputs built from the reference's own dequantize_tensor."""
+    from llada_quant_b200 import ops
+    E, H, I, T, K = (int(v) for v in golden["moe/shape"])
+    bits = int(golden[f"{name}/bits"])
+    x = torch.from_numpy(S.from_bf16_bits(golden["moe/x"])).to(torch.bfloat16).cuda()
+    t = lambda a: torch.from_numpy(golden[a]).cuda()
+    out = ops.fused_moe_packed(x, t(f"{name}/qw1"), t(f"{name}/sw1"), t(f"{name}/qw2"),
+                               t(f"{name}/sw2"), t("moe/topk_w"), t("moe/topk_ids"), bits,
+                               _impl_or_skip(impl))
+    _assert_layer_close(to_np(out), S.from_bf16_bits(golden[f"{name}/out"]))
+
+
+@pytest.mark.parametrize("impl", IMPLS)
+def test_gemm_stages_match_oracle(impl):
+    """GEMM1 (SiLU epilogue) and GEMM2 (routed weight, scatter) separately."""
+    from llada_quant_b200 import ops
+    T, E, H, I, k, bits = 256, 64, 2048, 1024, 8, 4
+    r1, r2 = _quantize(E, H, I, bits)
+    x = synthetic_tokens(T, H)
+    tw, ids = random_routing(T, E, k, seed=5)
+    offsets, slots = ops.moe_align(torch.from_numpy(ids).cuda(), E)
+    xs = ops.moe_permute(x.cuda(), slots, k)
+    h = ops.moe_gemm1(xs, offsets, r1.q, r1.scale, bits, _impl_or_skip(impl))
+    _, inter = M.fused_moe_packed(to_np(x), to_np(r1.q), to_np(r1.scale), to_np(r2.q),
+                                  to_np(r2.scale), tw, ids, bits, return_intermediates=True)
+    assert M.rel_l2(to_np(h), inter["h_sorted"]) <= 2e-3
+    # GEMM2 from the oracle's h so the two stages are judged independently
+    h_ref = torch.from_numpy(inter["h_sorted"]).to(torch.bfloat16).cuda()
+    y = ops.moe_gemm2(h_ref, offsets, slots, torch.from_numpy(tw).cuda(), r2.q, r2.scale, bits,
+                      _impl_or_skip(impl))
+    assert M.rel_l2(to_np(y), inter["y_slots"]) <= 2e-3
+
+
+def test_block_packed_mode_end_to_end():
+    """A fused expert block quantized in PACKED mode: w1 per access == reference dequant,
+    and the block's forward through fused_moe matches the oracle."""
+    import torch.nn as nn
+    from llada_quant_b200 import moe as RM
+    from llada_quant_b200.fused_moe import fused_moe, moe_layer
+
+    class Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            w1, w2 = synthetic_layer(16, 1024, 512)
+            self.w1 = nn.Parameter(w1.cuda())
+            self.w2 = nn.Parameter(w2.cuda())
+            self.gate_w = (torch.randn(16, 1024) * 0.02).to(torch.bfloat16).cuda()
+
+    b = Block()
+    weights = RM.QuantExpertWeights.quantize(b.w1.detach(), b.w2.detach(), bits=4, group_size=128)
+    RM.attach_packed_buffers(b, weights, torch.bfloat16)
+    RM.install_packed_expert_access(b)
+    assert RM.is_packed_expert_block(b)
+    a, c = b.w1, b.w1
+    assert torch.equal(a, c) and a.data_ptr() != c.data_ptr()
+    ref_w1 = S.dequantize_tensor(to_np(b._qw1), to_np(b._sw1), 4, 128, packed=True, to_bf16=True)
+    assert np.array_equal(to_np(a), ref_w1)
+    x = synthetic_tokens(64, 1024).cuda()
+    out = moe_layer(x, b.gate_w, b.packed_experts(), top_k=2)
+    out_ref, *_ = M.moe_layer(to_np(x), to_np(b.gate_w), to_np(b._qw1), to_np(b._sw1),
+                              to_np(b._qw2), to_np(b._sw2), 2, 4)
+    # routing may legitimately differ on near-tied logits; compare the layer via the
+    # same ids through fused_moe as well
+    logits = (x.float() @ b.gate_w.float().t()).to(torch.bfloat16)
+    tw, ids = torch.topk(torch.softmax(logits.float(), -1), 2)
+    out2 = fused_moe(x, b.packed_experts(), None, logits, ids.int())
+    ref2 = M.fused_moe_packed(to_np(x), to_np(b._qw1), to_np(b._sw1), to_np(b._qw2), to_np(b._sw2),
+                              to_np(tw), to_np(ids).astype(np.int32), 4)
+    _assert_layer_close(to_np(out2), ref2)
+    assert M.rel_l2(to_np(out), out_ref) < 0.05

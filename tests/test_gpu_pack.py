@@ -1,0 +1,122 @@
+"""GPU parity of quantize-and-pack, MSE search, dequantize and int4 (un)packing.
+
+Bar: bit-exact codes, packed bytes and scales against the reference's golden
+vectors and the oracle (amax); MSE scales bit-exact except at near-ties of the
+reference's own float32 group sums, each of which is verified to be one.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import symmetric as S
+from tests._util import to_np
+
+pytestmark = pytest.mark.gpu
+
+DT = {"bfloat16": torch.bfloat16, "float16": torch.float16, "float32": torch.float32}
+
+
+def _golden_input(golden, name):
+    w = torch.from_numpy(golden[f"{name}/w"]).to(DT[str(golden[f"{name}/dtype"])]).cuda()
+    bits, gs, mse, eff, packed = (int(v) for v in golden[f"{name}/meta"])
+    return w, bits, gs, mse, eff, packed
+
+
+@pytest.mark.parametrize("name", [
+    "amax_i4_g128_bf16", "amax_i8_g128_bf16", "amax_i4_g64_fp16", "amax_i8_g32_fp32",
+    "amax_i4_rowfallback", "amax_i8_rowfallback", "amax_i4_zero_groups",
+])
+def test_amax_pack_bit_exact_vs_reference_golden(golden, name):
+    from llada_quant_b200 import symmetric as G
+    w, bits, gs, _, eff, packed = _golden_input(golden, name)
+    r = G.quantize_tensor(w, bits=bits, group_size=gs)
+    assert r.group_size == eff and int(r.packed) == packed
+    assert np.array_equal(to_np(r.q), golden[f"{name}/q"])
+    assert np.array_equal(to_np(r.scale).view(np.uint32), golden[f"{name}/scale"].view(np.uint32))
+    deq = r.dequantize(torch.bfloat16)
+    assert np.array_equal(deq.cpu().view(torch.int16).numpy().view(np.uint16), golden[f"{name}/deq_bf16"])
+
+
+@pytest.mark.parametrize("name", ["mse_i4_g128_heavy", "mse_i8_g128_heavy", "mse_i4_g128_bf16",
+                                  "mse_i4_zero_groups"])
+def test_mse_pack_vs_reference_golden(golden, name):
+    from llada_quant_b200 import symmetric as G
+    w, bits, gs, _, eff, packed = _golden_input(golden, name)
+    r = G.quantize_tensor(w, bits=bits, group_size=gs, scale_search="mse")
+    ours, ref = to_np(r.scale), golden[f"{name}/scale"]
+    flips = ours.view(np.uint32) != ref.view(np.uint32)
+    w_g, _ = S.as_groups(golden[f"{name}/w"].astype(np.float32), gs)
+    for idx in zip(*np.nonzero(flips)):
+        e_ours = S.group_sse_terms(w_g[idx], np.float32(ours[idx]), bits).astype(np.float64).sum()
+        e_ref = S.group_sse_terms(w_g[idx], np.float32(ref[idx]), bits).astype(np.float64).sum()
+        assert abs(e_ours - e_ref) <= 1e-5 * max(e_ref, 1e-30), (idx, e_ours, e_ref)
+    assert flips.mean() <= 0.01
+    if not flips.any():
+        assert np.array_equal(to_np(r.q), golden[f"{name}/q"])
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("search", ["amax", "mse"])
+def test_pack_vs_oracle_on_expert_shaped_tensor(bits, search):
+    """C1-shaped w1 [16, 1024, 1024] bf16: amax bit-exact; MSE vs the oracle's exact-sum choice."""
+    from llada_quant_b200 import symmetric as G
+    g = torch.Generator().manual_seed(0)
+    w = (torch.randn(16, 1024, 1024, generator=g) * 0.02).to(torch.bfloat16)
+    if search == "mse":
+        w = w[:2]
+    r = G.quantize_tensor(w.cuda(), bits=bits, group_size=128, scale_search=search)
+    q, s, eff, packed, _ = S.quantize_tensor(w.float().numpy(), bits=bits, group_size=128,
+                                             scale_search=search)
+    ours = to_np(r.scale)
+    flips = ours.view(np.uint32) != s.view(np.uint32)
+    if search == "amax":
+        assert not flips.any()
+        assert np.array_equal(to_np(r.q), q)
+    else:
+        assert flips.mean() < 1e-3
+        same_rows = ~flips.any(axis=-1)
+        assert np.array_equal(to_np(r.q)[same_rows], q[same_rows])
+
+
+def test_search_errors_are_the_reference_terms():
+    """Each candidate's error equals the exact sum of the reference's rounded terms to fp32 accuracy."""
+    from llada_quant_b200 import ops
+    g = torch.Generator().manual_seed(4)
+    w = (torch.randn(8, 512, generator=g) * 0.02)
+    errs = to_np(ops.search_errors(w.cuda(), 4, 128, 24, 0.5))
+    _, ref = S.search_group_scale(S.as_groups(w.numpy(), 128)[0], 4, return_errors=True)
+    np.testing.assert_allclose(errs, ref, rtol=2e-6, atol=0)
+
+
+def test_unpack_every_byte_and_pack_every_pair(golden):
+    from llada_quant_b200 import symmetric as G
+    every = torch.arange(-128, 128, dtype=torch.int8).reshape(1, 256).cuda()
+    assert np.array_equal(to_np(G.unpack_int4(every)), golden["unpack_every_byte"])
+    pairs = torch.from_numpy(golden["pack_every_pair_in"]).cuda()
+    assert np.array_equal(to_np(G.pack_int4(pairs)), golden["pack_every_pair_out"])
+    with pytest.raises(ValueError, match=r"\[-8, 7\]"):
+        G.pack_int4(torch.tensor([[8, 0]], dtype=torch.int8).cuda())
+
+
+def test_dequantize_without_the_packed_flag_fails_loudly():
+    from llada_quant_b200 import symmetric as G
+    w = torch.randn(2, 4, 32).cuda()
+    r = G.quantize_tensor(w, bits=4, group_size=16)
+    with pytest.raises(RuntimeError):
+        G.dequantize_tensor(r.q, r.scale, 4, 16, packed=False)
+    assert G.dequantize_tensor(r.q, r.scale, 4, 16, packed=True).shape == w.shape
+
+
+def test_zero_tensor_and_scale_dtype():
+    from llada_quant_b200 import symmetric as G
+    r = G.quantize_tensor(torch.zeros(4, 8, 16).cuda(), bits=8, group_size=8)
+    assert torch.all(r.q == 0) and torch.all(r.scale == 0)
+    w = torch.randn(4, 256).cuda() * 0.1
+    rb = G.quantize_tensor(w, bits=4, group_size=64, scale_dtype=torch.bfloat16)
+    assert rb.scale.dtype == torch.bfloat16
+    q, s, *_ = S.quantize_tensor(w.cpu().numpy(), bits=4, group_size=64)
+    # the bf16 scale is the fp32 amax scale rounded once
+    assert np.array_equal(rb.scale.float().cpu().numpy(), S.round_to_bf16(s))
