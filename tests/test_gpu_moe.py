@@ -27,6 +27,16 @@ pytestmark = pytest.mark.gpu
 IMPLS = ["simt", "tcgen05"]
 
 
+@pytest.fixture(autouse=True)
+def _no_device_timeouts():
+    """Every bounded wait inside the tcgen05 kernels must have completed normally."""
+    from llada_quant_b200 import ops
+    ops.clear_device_error()
+    yield
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0, f"device error word {ops.device_error():#x}"
+
+
 def _impl_or_skip(impl):
     from llada_quant_b200 import _lib
     if impl == "tcgen05":
