@@ -124,40 +124,54 @@ class ClockSampler:
                 "samples": len(self.rows)}
 
 
+_CPU_CASE = {}
+
+
+def _cpu_case():
+    """Seeded C3 layer for the CPU path, quantized once by the oracle (not timed)."""
+    if not _CPU_CASE:
+        import torch
+        from oracle import symmetric as S
+        g = torch.Generator().manual_seed(0)
+        w1 = (torch.randn(E, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
+        q1, s1, *_ = S.quantize_tensor(w1, bits=BITS, group_size=GROUP)
+        del w1
+        w2 = (torch.randn(E, H, I, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
+        q2, s2, *_ = S.quantize_tensor(w2, bits=BITS, group_size=GROUP)
+        del w2
+        gate_w = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
+        x = torch.randn(T_PER_RANK, H, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).float().numpy()
+        _CPU_CASE.update(q1=q1, s1=s1, q2=q2, s2=s2, gate_w=gate_w, x=x)
+    return _CPU_CASE
+
+
 def cpu_reference(sample_layers: int = 1, threads=None):
-    """Time the reference CPU path (numpy port) on a bounded sample: ``sample_layers`` C3 layer
-    calls, each dequantizing every expert (what the PACKED property does) then the routed
-    dequant-then-matmul.  Returns (tokens/s, cores, seconds)."""
-    import numpy as np
-    import torch
+    """Time the reference CPU path (numpy port, oracle/moe.py) on a bounded sample:
+    ``sample_layers`` C3 layer calls of 256 tokens, each dequantizing every expert (what
+    the PACKED property does) and running the routed dequant-then-matmul.
+    Returns (tokens/s, cores, seconds)."""
     from threadpoolctl import threadpool_limits
-
     from oracle import moe as M
-    from oracle import symmetric as S
 
+    c = _cpu_case()
     cores = threads or os.cpu_count()
-    g = torch.Generator().manual_seed(0)
-    w1 = (torch.randn(E, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
-    w2 = (torch.randn(E, H, I, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
-    q1, s1, *_ = S.quantize_tensor(w1, bits=BITS, group_size=GROUP)
-    q2, s2, *_ = S.quantize_tensor(w2, bits=BITS, group_size=GROUP)
-    del w1, w2
-    gate_w = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
-    x = torch.randn(T_PER_RANK, H, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).float().numpy()
     with threadpool_limits(limits=cores):
         t0 = time.perf_counter()
         for _ in range(sample_layers):
-            M.moe_layer(x, gate_w, q1, s1, q2, s2, TOPK, BITS)
+            M.moe_layer(c["x"], c["gate_w"], c["q1"], c["s1"], c["q2"], c["s2"], TOPK, BITS)
         dt = time.perf_counter() - t0
     return sample_layers * T_PER_RANK / dt, cores, dt
 
 
 def run_reference(args, rank: int):
+    """The reference arm: rank 0 times the CPU path; warm-up is capped at one call (it only
+    faults pages in) so that the whole run stays within a few minutes."""
     if rank != 0:
         return
     vals = []
-    for _ in range(args.warmup):
+    for _ in range(min(args.warmup, 1)):
         cpu_reference(1)
+    cores = os.cpu_count()
     for _ in range(args.steps):
         v, cores, dt = cpu_reference(1)
         vals.append(v)
@@ -167,11 +181,11 @@ def run_reference(args, rank: int):
         "warmup": args.warmup, "ms_per_step": T_PER_RANK / value * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, bf16 activations, fp32 accumulate",
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) tokens)", "impl": "reference",
-        "config": {"workload": "C3 LLaDA-MoE-7B-A1B layer: E=64 H=2048 I=1024 top-8 W4A16 g128, "
-                               "T=256 tokens per call", "tokens_per_step": T_PER_RANK},
+        "config": {"workload": "C3 LLaDA-MoE-7B-A1B layer: E=64 H=2048 I=1024 top-8 W4A16 g128",
+                   "tokens_per_step": T_PER_RANK},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": "one C3 layer call per step (numpy port of the reference's "
-                                   "PACKED dequantize + routed dequant-then-matmul)"},
+                         "sample": "one C3 layer call (256 tokens) per step: numpy port of the "
+                                   "reference's PACKED dequantize + routed dequant-then-matmul"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -348,6 +362,28 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         print(json.dumps(line), flush=True)
 
 
+def kernel_case(args):
+    """One C3 layer weight set, route -> align -> permute -> GEMM1 -> GEMM2 -> combine, twice."""
+    import torch
+    from llada_quant_b200 import ops
+    from llada_quant_b200.fused_moe import IMPL
+    device = torch.device("cuda", 0)
+    layers, gate_w = make_layers(device, 1, E, 0)
+    lay = layers[0]
+    x = torch.randn(T_PER_RANK, H, generator=torch.Generator(device=device).manual_seed(2),
+                    device=device).to(torch.bfloat16)
+    impl = IMPL[args.gemm]
+    for _ in range(2):
+        tw, ids, _ = ops.route(x, gate_w, TOPK, None, False)
+        off, slots = ops.moe_align(ids, E)
+        xs = ops.moe_permute(x, slots, TOPK)
+        h = ops.moe_gemm1(xs, off, lay.qw1, lay.sw1, BITS, impl)
+        y = ops.moe_gemm2(h, off, slots, tw, lay.qw2, lay.sw2, BITS, impl)
+        out = ops.moe_combine(y, TOPK)
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel_case": "C3", "gemm": args.gemm, "out_abs_mean": float(out.float().abs().mean())}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -356,7 +392,13 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--gemm", choices=["auto", "tcgen05", "simt"], default="auto")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--kernel-case", action="store_true",
+                    help="run the C3 layer's kernels twice on one small input set and exit "
+                         "(the command the ncu captures under profiles/ were taken on)")
     args = ap.parse_args()
+    if args.kernel_case:
+        kernel_case(args)
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
