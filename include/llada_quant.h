@@ -178,6 +178,22 @@ int llq_fused_moe_packed(const void* x, const int8_t* qw1, const float* sw1, con
                          void* stream);
 
 /*
+ * No counterpart in the reference.  The same layer as llq_fused_moe_packed for
+ * callers that cannot allocate device memory (a plugin inside a framework that
+ * owns the allocator, a runtime that reserves all memory at start-up): no
+ * workspace argument, and the library allocates nothing either.  Its scratch is
+ * one fixed device array of about 12 MiB inside the library, held on every GPU
+ * that loads it until exit.  Limits: T*k <= 2048, H <= 2048, I <= 1024,
+ * E <= 256; larger calls return LLQ_EINVAL.  The first call on a device sets
+ * up the array's address there -- make it before any stream capture.  All
+ * calls share the array: calls whose GPU executions overlap race.
+ */
+int llq_fused_moe_packed_noalloc(const void* x, const int8_t* qw1, const float* sw1,
+                                 const int8_t* qw2, const float* sw2, const float* topk_w,
+                                 const int32_t* topk_ids, int64_t T, int E, int H, int I, int k,
+                                 int bits, int group_size, void* out, int impl, void* stream);
+
+/*
  * Device error word written by bounded waits inside the tcgen05 kernels
  * (0 = none).  Reading it synchronizes the device.  llq_clear_device_error
  * resets it.

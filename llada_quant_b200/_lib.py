@@ -42,6 +42,7 @@ SIGNATURES = {
     "llq_moe_gemm2": (I, [P, P, P, P, L, I, I, I, P, P, I, I, P, I, P]),
     "llq_moe_workspace_size": (c_size_t, [L, I, I, I, I]),
     "llq_fused_moe_packed": (I, [P, P, P, P, P, P, P, L, I, I, I, I, I, I, P, P, c_size_t, I, P]),
+    "llq_fused_moe_packed_noalloc": (I, [P, P, P, P, P, P, P, L, I, I, I, I, I, I, P, I, P]),
     "llq_device_error": (I, [P]),
     "llq_clear_device_error": (I, []),
 }
