@@ -390,7 +390,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--gemm", choices=["auto", "tcgen05", "simt"], default="auto")
+    ap.add_argument("--gemm", choices=["auto", "tcgen05", "tcgen05_fast", "simt"], default="auto")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--kernel-case", action="store_true",
                     help="run the C3 layer's kernels twice on one small input set and exit "

@@ -43,7 +43,19 @@ enum llq_dtype { LLQ_F32 = 0, LLQ_F16 = 1, LLQ_BF16 = 2 };
 
 enum llq_scale_search { LLQ_SEARCH_AMAX = 0, LLQ_SEARCH_MSE = 1 };
 
-enum llq_gemm_impl { LLQ_GEMM_AUTO = 0, LLQ_GEMM_TCGEN05 = 1, LLQ_GEMM_SIMT = 2 };
+/*
+ * Expert GEMM implementation.  AUTO = TCGEN05 where it covers the shape, else
+ * SIMT.  TCGEN05 and SIMT use weights bit-identical to dequantize_tensor.
+ * TCGEN05_FAST (INT4, whole-layer calls only) feeds the integer codes to the
+ * tensor cores and applies each fp32 group scale to the group's fp32 partial
+ * sum: W = q * s without the per-weight bf16 rounding.
+ */
+enum llq_gemm_impl {
+  LLQ_GEMM_AUTO = 0,
+  LLQ_GEMM_TCGEN05 = 1,
+  LLQ_GEMM_SIMT = 2,
+  LLQ_GEMM_TCGEN05_FAST = 3
+};
 
 /* Library version (major*10000 + minor*100 + patch). */
 int llq_version(void);

@@ -17,7 +17,7 @@ LIB_PATH = os.path.join(HERE, "libllada_quant_cuda.so")
 LLQ_OK, LLQ_EINVAL, LLQ_EUNSUPPORTED, LLQ_ECUDA, LLQ_ETIMEOUT, LLQ_ENOSPACE = range(6)
 LLQ_F32, LLQ_F16, LLQ_BF16 = 0, 1, 2
 LLQ_SEARCH_AMAX, LLQ_SEARCH_MSE = 0, 1
-LLQ_GEMM_AUTO, LLQ_GEMM_TCGEN05, LLQ_GEMM_SIMT = 0, 1, 2
+LLQ_GEMM_AUTO, LLQ_GEMM_TCGEN05, LLQ_GEMM_SIMT, LLQ_GEMM_TCGEN05_FAST = 0, 1, 2, 3
 
 P = c_void_p
 I = c_int

@@ -42,16 +42,16 @@ int route_topk_impl(const void*, int, int64_t, int, int, const float*, int, floa
                     cudaStream_t);
 size_t align_workspace_size(int64_t, int, int);
 int align_impl(const int32_t*, int64_t, int, int, int32_t*, int32_t*, void*, size_t, cudaStream_t);
-int permute_impl(const void*, int64_t, int, int, const int32_t*, void*, cudaStream_t);
+int permute_impl(const void*, int64_t, int, int, const int32_t*, void*, cudaStream_t, int);
 int combine_impl(const void*, int64_t, int, int, void*, cudaStream_t);
 int gemm1_simt(const void*, const int32_t*, int, int, int, const int8_t*, const float*, int, int,
                void*, cudaStream_t);
 int gemm2_simt(const void*, const int32_t*, const int32_t*, const float*, int, int, int,
                const int8_t*, const float*, int, int, void*, cudaStream_t);
 int gemm1_tc(const void*, const int32_t*, int64_t, int, int, int, const int8_t*, const float*, int,
-             int, void*, cudaStream_t);
+             int, void*, bool, cudaStream_t);
 int gemm2_tc(const void*, const int32_t*, const int32_t*, const float*, int64_t, int, int, int,
-             const int8_t*, const float*, int, int, void*, cudaStream_t);
+             const int8_t*, const float*, int, int, void*, bool, cudaStream_t);
 bool tc_supported(int E, int N_out, int K, int bits, int group_size, bool gemm1);
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -91,6 +91,8 @@ int pick_impl(int impl, int E, int N_out, int K, int bits, int group_size, bool 
   if (impl == LLQ_GEMM_SIMT) return LLQ_GEMM_SIMT;
   const bool tc = tc_supported(E, N_out, K, bits, group_size, gemm1);
   if (impl == LLQ_GEMM_TCGEN05) return tc ? LLQ_GEMM_TCGEN05 : -1;
+  if (impl == LLQ_GEMM_TCGEN05_FAST) return (tc && bits == 4) ? LLQ_GEMM_TCGEN05_FAST : -1;
+  if (impl != LLQ_GEMM_AUTO) return -1;
   return tc ? LLQ_GEMM_TCGEN05 : LLQ_GEMM_SIMT;
 }
 
@@ -153,7 +155,7 @@ int llq_moe_align(const int32_t* topk_ids, int64_t T, int k, int E, int32_t* exp
 
 int llq_moe_permute(const void* x, int64_t T, int H, int k, const int32_t* sorted_slots, void* x_sorted,
                     void* stream) {
-  return permute_impl(x, T, H, k, sorted_slots, x_sorted, as_stream(stream));
+  return permute_impl(x, T, H, k, sorted_slots, x_sorted, as_stream(stream), 0);
 }
 
 int llq_moe_combine(const void* y_slots, int64_t T, int k, int H, void* out, void* stream) {
@@ -163,11 +165,13 @@ int llq_moe_combine(const void* y_slots, int64_t T, int k, int H, void* out, voi
 int llq_moe_gemm1(const void* x_sorted, const int32_t* expert_offsets, int64_t n_rows, int E, int H,
                   int I, const int8_t* qw1, const float* sw1, int bits, int group_size,
                   void* h_sorted, int impl, void* stream) {
+  if (impl == LLQ_GEMM_TCGEN05_FAST)
+    return fail(LLQ_EUNSUPPORTED, "LLQ_GEMM_TCGEN05_FAST needs K-permuted activations: use llq_fused_moe_packed");
   const int which = pick_impl(impl, E, I, H, bits, group_size, true);
   if (which < 0) return fail(LLQ_EUNSUPPORTED, "tcgen05 GEMM1 does not cover this shape");
   if (which == LLQ_GEMM_TCGEN05)
     return gemm1_tc(x_sorted, expert_offsets, n_rows, E, H, I, qw1, sw1, bits, group_size,
-                    h_sorted, as_stream(stream));
+                    h_sorted, false, as_stream(stream));
   return gemm1_simt(x_sorted, expert_offsets, E, H, I, qw1, sw1, bits, group_size, h_sorted,
                     as_stream(stream));
 }
@@ -175,11 +179,13 @@ int llq_moe_gemm1(const void* x_sorted, const int32_t* expert_offsets, int64_t n
 int llq_moe_gemm2(const void* h_sorted, const int32_t* expert_offsets, const int32_t* sorted_slots,
                   const float* topk_w, int64_t n_rows, int E, int H, int I, const int8_t* qw2,
                   const float* sw2, int bits, int group_size, void* y_slots, int impl, void* stream) {
+  if (impl == LLQ_GEMM_TCGEN05_FAST)
+    return fail(LLQ_EUNSUPPORTED, "LLQ_GEMM_TCGEN05_FAST needs K-permuted activations: use llq_fused_moe_packed");
   const int which = pick_impl(impl, E, H, I, bits, group_size, false);
   if (which < 0) return fail(LLQ_EUNSUPPORTED, "tcgen05 GEMM2 does not cover this shape");
   if (which == LLQ_GEMM_TCGEN05)
     return gemm2_tc(h_sorted, expert_offsets, sorted_slots, topk_w, n_rows, E, H, I, qw2, sw2,
-                    bits, group_size, y_slots, as_stream(stream));
+                    bits, group_size, y_slots, false, as_stream(stream));
   return gemm2_simt(h_sorted, expert_offsets, sorted_slots, topk_w, E, H, I, qw2, sw2, bits,
                     group_size, y_slots, as_stream(stream));
 }
@@ -202,7 +208,21 @@ int llq_fused_moe_packed(const void* x, const int8_t* qw1, const float* sw1, con
   const int64_t n = T * k;
   int rc = align_impl(topk_ids, T, k, E, ws.offsets, ws.sorted_slots, ws.align_ws, ws.align_bytes, st);
   if (rc) return rc;
-  rc = permute_impl(x, T, H, k, ws.sorted_slots, ws.x_sorted, st);
+  if (impl == LLQ_GEMM_TCGEN05_FAST) {
+    if (pick_impl(impl, E, I, H, bits, group_size, true) < 0 ||
+        pick_impl(impl, E, H, I, bits, group_size, false) < 0)
+      return fail(LLQ_EUNSUPPORTED, "LLQ_GEMM_TCGEN05_FAST does not cover this shape (INT4, K <= 2048, "
+                                    "I %% 128 == 0, H %% 256 == 0, group %% 128 == 0)");
+    rc = permute_impl(x, T, H, k, ws.sorted_slots, ws.x_sorted, st, 1);
+    if (rc) return rc;
+    rc = gemm1_tc(ws.x_sorted, ws.offsets, n, E, H, I, qw1, sw1, bits, group_size, ws.h_sorted, true, st);
+    if (rc) return rc;
+    rc = gemm2_tc(ws.h_sorted, ws.offsets, ws.sorted_slots, topk_w, n, E, H, I, qw2, sw2, bits, group_size,
+                  ws.y_slots, true, st);
+    if (rc) return rc;
+    return combine_impl(ws.y_slots, T, k, H, out, st);
+  }
+  rc = permute_impl(x, T, H, k, ws.sorted_slots, ws.x_sorted, st, 0);
   if (rc) return rc;
   rc = llq_moe_gemm1(ws.x_sorted, ws.offsets, n, E, H, I, qw1, sw1, bits, group_size, ws.h_sorted,
                      impl, stream);

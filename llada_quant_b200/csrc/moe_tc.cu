@@ -1,26 +1,37 @@
 // tcgen05 grouped expert GEMMs over the packed LLaDA_Quant buffers (sm_100a).
 //
-// Shape of the work (swap-AB): the MMA's M side is 128 weight rows of one
-// expert, its N side is that expert's routed tokens (16..128 per tile), K runs
-// over the hidden (GEMM1) or intermediate (GEMM2) dimension in chunks of 128.
+// Persistent kernel: one CTA per SM walks a compacted list of work items
+// (expert, token tile, 256-row block).  Per item the MMA's M side is two
+// 128-row weight tiles -- gate and up rows for GEMM1 (so the SiLU epilogue is
+// thread-local), two consecutive 128-row blocks of w2 for GEMM2 -- and its N
+// side is up to NTM of the expert's routed tokens.  K runs in steps of 128.
 //
-//   warp 0      TMA producer: packed weight tile(s) [128 rows x 64/128 bytes]
-//               and the token tile [N rows x 128 bf16] into a 4-stage SMEM ring
-//   warp 1      TMEM allocator and MMA issuer (one thread):
+//   warp 0      TMA producer: per item the fp32 scales of both tiles (one bulk
+//               copy each, double-buffered), per step both packed weight tiles
+//               [128 rows x 64/128 B] and the token tile [N x 128] bf16
+//   warp 1      TMEM allocator + MMA issuer (one thread):
 //               tcgen05.mma.cta_group::1.kind::f16, A from TMEM, B from SMEM
-//   warps 2-9   dequantize: packed nibbles/bytes + fp32 group scale ->
-//               bf16(q * s) exactly as dequantize_tensor
-//               (src/LLaDA_Quant/algorithms/symmetric.py:286-293), written to
-//               TMEM with tcgen05.st as the MMA's A operand; then the epilogue
-//               (tcgen05.ld of the fp32 accumulators):
-//                 GEMM1  h = bf16(bf16(silu(bf16(gate))) * bf16(up))
-//                        (INFERENCE_REPO_CHANGES.md:296-309)
-//                 GEMM2  y[slot] = bf16(acc * topk_w[slot])  (:259-265)
+//   warps 2-9   dequantize into TMEM (tcgen05.st) as the MMA's A operand
+//   warps 10-17 epilogue (tcgen05.ld of the accumulators)
 //
-// The dequantized weights never touch HBM or SMEM: packed bytes stream
-// HBM -> SMEM (TMA) -> registers -> TMEM.  No TMA multicast is used.
-// Every mbarrier wait is bounded (about 2 s); on timeout the kernel records
-// LLQ_ETIMEOUT-class codes in g_device_error, drains, frees TMEM and exits.
+// Two dequantization modes:
+//   exact  A = bf16(fp32(q) * s), bit-identical to dequantize_tensor
+//          (src/LLaDA_Quant/algorithms/symmetric.py:286-293); one fp32
+//          accumulator per tile over all of K.
+//   fast   (INT4) A = q, the integer code, exact in bf16; the MMA writes one
+//          fp32 partial sum per 128-group into a double-buffered TMEM slot and
+//          the epilogue warps accumulate s_g * partial_g in fp32 registers --
+//          the quantization contract W = q * s without rounding each weight to
+//          bf16.  Codes are written in the order (k0,k4),(k1,k5),(k2,k6),(k3,k7)
+//          of each 8-element block, so the token operand must be permuted the
+//          same way (moe_permute with kperm, and GEMM1's epilogue for GEMM2).
+// Epilogues follow the external fused_moe's rounding order:
+//   GEMM1  h = bf16(bf16(silu(bf16(gate))) * bf16(up))  (INFERENCE_REPO_CHANGES.md:296-309)
+//   GEMM2  y[slot] = bf16(acc * topk_w[slot])            (:259-265)
+//
+// No TMA multicast is used.  Every mbarrier wait is bounded (~2 s of SM
+// clocks); on timeout the kernel records a code in g_device_error, drains its
+// copies (bounded), frees TMEM and exits.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -30,29 +41,37 @@ namespace llq {
 
 namespace {
 
-constexpr int KC = 128;        // K elements per pipeline step
-constexpr int NT_MAX = 128;    // tokens per tile (MMA N <= 128)
-constexpr int ROWS = 128;      // weight rows per MMA (M)
-constexpr int DQ_WARPS = 8;    // two warpgroups of dequant/epilogue warps
-constexpr int THREADS = 64 + DQ_WARPS * 32;
+constexpr int KC = 128;
+constexpr int ROWS = 128;
+constexpr int DQ_WARPS = 8;
+constexpr int EPI_WARPS = 8;
+constexpr int FIRST_DQ = 2;
+constexpr int FIRST_EPI = FIRST_DQ + DQ_WARPS;
+constexpr int THREADS = (FIRST_EPI + EPI_WARPS) * 32;  // 576
 constexpr uint32_t TMEM_COLS = 512;
-constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 2 GHz
+constexpr int MAX_G = 16;  // scale groups per row (K <= 2048 at group 128)
+constexpr int MAX_E = 256;
+constexpr long long kTimeoutCycles = 4000000000LL;
 
-template <bool GEMM1, int BITS>
+template <bool GEMM1, int BITS, bool FAST, int NTM>
 struct Cfg {
-  static constexpr int W_ROW_BYTES = KC * BITS / 8;             // 64 (int4) or 128 (int8)
-  static constexpr int W_TILES = GEMM1 ? 2 : 1;                  // gate + up, or w2
+  static constexpr int W_ROW_BYTES = KC * BITS / 8;
   static constexpr int W_TILE_BYTES = ROWS * W_ROW_BYTES;
-  static constexpr int W_STAGE_BYTES = W_TILES * W_TILE_BYTES;
-  static constexpr int B_STAGE_BYTES = NT_MAX * KC * 2;
-  static constexpr int STAGES = (GEMM1 && BITS == 8) ? 3 : 4;
-  static constexpr int ACC_COLS = W_TILES * NT_MAX;
-  static constexpr int A_STAGE_COLS = W_TILES * KC / 2;          // bf16 pairs per lane
-  static constexpr int A_STAGES_FIT = (int)(TMEM_COLS - ACC_COLS) / A_STAGE_COLS;
+  static constexpr int W_STAGE_BYTES = 2 * W_TILE_BYTES;
+  static constexpr int B_STAGE_BYTES = NTM * KC * 2;
+  static constexpr int STAGE_BYTES = W_STAGE_BYTES + B_STAGE_BYTES;
+  static constexpr int SCALE_BUF_BYTES = 2 * ROWS * MAX_G * 4;
+  static constexpr int STAGES_FIT = (220 * 1024 - 2 * SCALE_BUF_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 4 ? 4 : STAGES_FIT;
+  static constexpr int ACC_COLS = FAST ? 4 * NTM : 2 * NTM;
+  static constexpr int A_STAGE_COLS = KC;  // 64 columns per tile
+  static constexpr int A_STAGES_FIT = static_cast<int>(TMEM_COLS - ACC_COLS) / A_STAGE_COLS;
   static constexpr int A_STAGES = A_STAGES_FIT > 4 ? 4 : A_STAGES_FIT;
-  static constexpr int CHUNKS = KC * BITS / 8 / 16;              // 16-byte chunks per row per step
+  static constexpr int CHUNKS = W_ROW_BYTES / 16;
   static constexpr size_t SMEM_BYTES =
-      1024 + static_cast<size_t>(STAGES) * (W_STAGE_BYTES + B_STAGE_BYTES) + 512;
+      1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + 2 * SCALE_BUF_BYTES + 2048;
+  static_assert(STAGES >= 2 && A_STAGES >= 2, "pipeline too shallow");
+  static_assert(!FAST || BITS == 4, "fast mode is INT4 only");
 };
 
 struct TcArgs {
@@ -61,10 +80,12 @@ struct TcArgs {
   const int32_t* sorted_slots;
   const float* topk_w;
   __nv_bfloat16* out;
+  int E;
   int K;           // reduction length (H for GEMM1, I for GEMM2)
   int rows_total;  // weight rows per expert (2I or H)
   int inter;       // I
   int n_out;       // output row length (I for GEMM1, H for GEMM2)
+  int rblocks;     // 256-row blocks per expert (I/128 for GEMM1, H/256 for GEMM2)
   int group;       // 0 = one scale per row
   int groups;      // scales per row
 };
@@ -127,6 +148,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -187,12 +215,13 @@ __device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr) {
 }
 
 // ---------------------------------------------------------------------------
-// exact dequantization: bf16(fp32(q) * s), two values per bf16x2 word
+// dequantization
 // ---------------------------------------------------------------------------
-// The integer is rebuilt as the float 2^23 + u (u = q + bias in the mantissa)
-// and the bias subtracted exactly; the high nibble is taken in place, i.e.
-// as 16 * q, and multiplied by s / 16 -- the same exact product, so the single
-// fp32 rounding and the bf16 rounding match q * s in dequantize_tensor.
+// exact: the integer is rebuilt as the float 2^23 + u (u = q + bias in the
+// mantissa, byte permute) and the bias subtracted exactly; the high nibble is
+// taken in place, i.e. as 16 * q, and multiplied by s / 16 -- the same exact
+// product -- so the single fp32 rounding and the bf16 rounding equal those of
+// q * s in dequantize_tensor.
 __device__ __forceinline__ uint32_t scale_pair_to_bf16x2(uint32_t lo_bits, uint32_t hi_bits, float c_lo,
                                                          float c_hi, float s_lo, float s_hi) {
   uint32_t o;
@@ -210,8 +239,8 @@ __device__ __forceinline__ uint32_t scale_pair_to_bf16x2(uint32_t lo_bits, uint3
   return o;
 }
 
-// 16 packed bytes = 32 int4 values -> 16 bf16x2 words (natural K order)
-__device__ __forceinline__ void dequant_int4_chunk(uint4 v, float s, uint32_t (&out)[16]) {
+// 16 packed bytes = 32 int4 values -> 16 bf16x2 words, natural K order
+__device__ __forceinline__ void dequant_int4_exact(uint4 v, float s, uint32_t (&out)[16]) {
   const float s16 = s * 0.0625f;
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -227,7 +256,7 @@ __device__ __forceinline__ void dequant_int4_chunk(uint4 v, float s, uint32_t (&
 }
 
 // 16 int8 values -> 8 bf16x2 words
-__device__ __forceinline__ void dequant_int8_chunk(uint4 v, float s, uint32_t* out) {
+__device__ __forceinline__ void dequant_int8_exact(uint4 v, float s, uint32_t* out) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -241,42 +270,106 @@ __device__ __forceinline__ void dequant_int8_chunk(uint4 v, float s, uint32_t* o
   }
 }
 
+// fast: integer codes as bf16.  (x & 0x000F000F) ^ 0x43084308 puts nibbles 0
+// and 4 into two bf16 mantissas as 128 + (q + 8); subtracting 136 leaves q
+// exactly.  Pairs come out as (k0,k4),(k1,k5),(k2,k6),(k3,k7).
+__device__ __forceinline__ uint32_t code_pair(uint32_t x) {
+  uint32_t t, o;
+  asm("lop3.b32 %0, %1, 0x000F000F, 0x43084308, 0x6A;" : "=r"(t) : "r"(x));
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(o) : "r"(t), "r"(0xC308C308u));
+  return o;
+}
+
+__device__ __forceinline__ void codes_int4(uint4 v, uint32_t (&out)[16]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    out[i * 4 + 0] = code_pair(w[i]);
+    out[i * 4 + 1] = code_pair(w[i] >> 4);
+    out[i * 4 + 2] = code_pair(w[i] >> 8);
+    out[i * 4 + 3] = code_pair(w[i] >> 12);
+  }
+}
+
+// position of feature n inside a K-permuted row (inverse of [0,4,1,5,2,6,3,7])
+__device__ __forceinline__ int kperm_pos(int n) {
+  const int j = n & 7;
+  return (n & ~7) | (j < 4 ? 2 * j : 2 * (j - 4) + 1);
+}
+
 __device__ __forceinline__ int box_index(int rows) {
   return rows <= 16 ? 0 : rows <= 32 ? 1 : rows <= 64 ? 2 : 3;
 }
 
+struct Item {
+  int e, tt, rb, row0, rows_t;
+};
+
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <bool GEMM1, int BITS>
+template <bool GEMM1, int BITS, bool FAST, int NTM>
 __global__ void __launch_bounds__(THREADS, 1)
     moe_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_b0,
                        const __grid_constant__ CUtensorMap tm_b1, const __grid_constant__ CUtensorMap tm_b2,
                        const __grid_constant__ CUtensorMap tm_b3, const TcArgs args) {
-  using C = Cfg<GEMM1, BITS>;
+  using C = Cfg<GEMM1, BITS, FAST, NTM>;
   constexpr int S = C::STAGES;
   constexpr int AS = C::A_STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sw = smem;
   uint8_t* sb = sw + S * C::W_STAGE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sb + S * C::B_STAGE_BYTES);
+  float* ssc = reinterpret_cast<float*>(sb + S * C::B_STAGE_BYTES);  // [2 bufs][2 tiles][128 * G]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(ssc) + 2 * C::SCALE_BUF_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = full + S;
   uint64_t* a_full = empty + S;
   uint64_t* a_empty = a_full + AS;
-  uint64_t* acc_full = a_empty + AS;
-  uint64_t* acc_empty = acc_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+  uint64_t* sc_full = a_empty + AS;     // [2]
+  uint64_t* sc_empty = sc_full + 2;     // [2]
+  uint64_t* acc_full = sc_empty + 2;    // [2] (exact uses [0])
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* tile_prefix = reinterpret_cast<int*>(tmem_slot + 2);  // [E + 1]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e = blockIdx.y, rb = blockIdx.x;
-  const int row0 = args.offsets[e];
-  const int m_e = args.offsets[e + 1] - row0;
-  if (m_e <= 0) return;  // uniform for the whole CTA, before any barrier or TMEM use
+  const int E = args.E;
+  const int G = args.groups;
+  const int kch = args.K / KC;
 
-  if (threadIdx.x == 0) {
+  // ---- compacted work list: token tiles per expert, prefix-summed by warp 0
+  if (warp == 0) {
+    int local[MAX_E / 32];
+    int sum = 0;
+#pragma unroll
+    for (int j = 0; j < MAX_E / 32; ++j) {
+      const int e = lane * (MAX_E / 32) + j;
+      int n = 0;
+      if (e < E) {
+        const int m = args.offsets[e + 1] - args.offsets[e];
+        n = (m + NTM - 1) / NTM;
+      }
+      local[j] = n;
+      sum += n;
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    int run = incl - sum;
+#pragma unroll
+    for (int j = 0; j < MAX_E / 32; ++j) {
+      const int e = lane * (MAX_E / 32) + j;
+      if (e < E) tile_prefix[e] = run;
+      run += local[j];
+    }
+    if (lane == 31) tile_prefix[E] = incl;
+  }
+  if (threadIdx.x == 32) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], DQ_WARPS + 1);
@@ -285,8 +378,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&a_full[i], DQ_WARPS);
       mbar_init(&a_empty[i], 1);
     }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, DQ_WARPS);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sc_full[i], 1);
+      mbar_init(&sc_empty[i], FAST ? DQ_WARPS + EPI_WARPS : DQ_WARPS);
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], EPI_WARPS);
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -301,156 +398,253 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int total_tiles = tile_prefix[E];
+  const int total_items = total_tiles * args.rblocks;
 
-  const int n_tiles = (m_e + NT_MAX - 1) / NT_MAX;
-  const int kch = args.K / KC;
-  const int total = n_tiles * kch;
-  const int64_t wrow_a = static_cast<int64_t>(e) * args.rows_total + static_cast<int64_t>(rb) * ROWS;
-  const int64_t wrow_b = wrow_a + args.inter;  // up rows (GEMM1 only)
+  auto item_at = [&](int u) -> Item {
+    Item it;
+    const int tg = u / args.rblocks;
+    it.rb = u - tg * args.rblocks;
+    int lo = 0, hi = E;  // largest e with tile_prefix[e] <= tg
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (tile_prefix[mid] <= tg) lo = mid; else hi = mid;
+    }
+    it.e = lo;
+    it.tt = tg - tile_prefix[lo];
+    const int base = args.offsets[lo];
+    const int m = args.offsets[lo + 1] - base;
+    it.row0 = base + it.tt * NTM;
+    it.rows_t = min(NTM, m - it.tt * NTM);
+    return it;
+  };
+  auto wrow_of = [&](const Item& it, int tile) -> int64_t {
+    if (GEMM1)
+      return static_cast<int64_t>(it.e) * args.rows_total + (tile ? args.inter : 0) +
+             static_cast<int64_t>(it.rb) * ROWS;
+    return static_cast<int64_t>(it.e) * args.rows_total + static_cast<int64_t>(it.rb) * 2 * ROWS + tile * ROWS;
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------- producer
     if (lane == 0) {
-      int issued = 0;
-      for (int it = 0; it < total; ++it) {
-        const int tile = it / kch, kc = it - tile * kch, s = it % S;
-        if (!mbar_wait(&empty[s], ((it / S) & 1) ^ 1, abort_flag, 0x100 + s)) break;
-        const int rows_t = min(NT_MAX, m_e - tile * NT_MAX);
-        const int bi = box_index(rows_t);
+      int it = 0, issued = 0;
+      bool ok = true;
+      for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
+        const Item item = item_at(u);
+        const int sbuf = ii & 1;
+        if (!mbar_wait(&sc_empty[sbuf], ((ii >> 1) & 1) ^ 1, abort_flag, 0x100)) break;
+        const uint32_t sbytes = static_cast<uint32_t>(ROWS * G * 4);
+        mbar_expect_tx(&sc_full[sbuf], 2 * sbytes);
+        float* sdst = ssc + sbuf * (2 * ROWS * MAX_G);
+        bulk_load(sdst, args.scale + wrow_of(item, 0) * G, sbytes, &sc_full[sbuf]);
+        bulk_load(sdst + ROWS * MAX_G, args.scale + wrow_of(item, 1) * G, sbytes, &sc_full[sbuf]);
+        const int bi = box_index(item.rows_t);
         const int box = 16 << bi;
-        mbar_expect_tx(&full[s], C::W_STAGE_BYTES + 2 * box * 128);
-        uint8_t* wdst = sw + s * C::W_STAGE_BYTES;
-        tma_load_2d(wdst, &tm_w, kc * C::W_ROW_BYTES, static_cast<int>(wrow_a), &full[s]);
-        if (GEMM1) tma_load_2d(wdst + C::W_TILE_BYTES, &tm_w, kc * C::W_ROW_BYTES, static_cast<int>(wrow_b), &full[s]);
         const CUtensorMap* tb = bi == 0 ? &tm_b0 : bi == 1 ? &tm_b1 : bi == 2 ? &tm_b2 : &tm_b3;
-        uint8_t* bdst = sb + s * C::B_STAGE_BYTES;
-        const int trow = row0 + tile * NT_MAX;
-        tma_load_2d(bdst, tb, kc * KC, trow, &full[s]);
-        tma_load_2d(bdst + box * 128, tb, kc * KC + 64, trow, &full[s]);
-        ++issued;
+        const int w0 = static_cast<int>(wrow_of(item, 0)), w1 = static_cast<int>(wrow_of(item, 1));
+        for (int kc = 0; kc < kch; ++kc, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(&empty[s], ((it / S) & 1) ^ 1, abort_flag, 0x110 + s)) { ok = false; break; }
+          mbar_expect_tx(&full[s], C::W_STAGE_BYTES + 2 * box * 128);
+          uint8_t* wdst = sw + s * C::W_STAGE_BYTES;
+          tma_load_2d(wdst, &tm_w, kc * C::W_ROW_BYTES, w0, &full[s]);
+          tma_load_2d(wdst + C::W_TILE_BYTES, &tm_w, kc * C::W_ROW_BYTES, w1, &full[s]);
+          uint8_t* bdst = sb + s * C::B_STAGE_BYTES;
+          tma_load_2d(bdst, tb, kc * KC, item.row0, &full[s]);
+          tma_load_2d(bdst + box * 128, tb, kc * KC + 64, item.row0, &full[s]);
+          ++issued;
+        }
       }
-      // drain: never leave the CTA with copies still landing in its shared memory
-      for (int it = (issued > S ? issued - S : 0); it < issued; ++it) {
-        long long t0 = clock64();
-        while (!mbar_try_wait(&full[it % S], (it / S) & 1) && clock64() - t0 < kTimeoutCycles) {
+      // never leave copies in flight into this CTA's shared memory
+      for (int i = (issued > S ? issued - S : 0); i < issued; ++i) {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(&full[i % S], (i / S) & 1) && clock64() - t0 < kTimeoutCycles) {
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t acc_a = tmem;                 // gate (GEMM1) or w2 accumulator
-      const uint32_t acc_b = tmem + NT_MAX;        // up accumulator (GEMM1)
       const uint32_t a_base = tmem + C::ACC_COLS;
-      for (int it = 0; it < total; ++it) {
-        const int tile = it / kch, kc = it - tile * kch, s = it % S, sa = it % AS;
-        if (kc == 0) {
-          if (!mbar_wait(acc_empty, (tile & 1) ^ 1, abort_flag, 0x200)) break;
-        }
-        if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, 0x210 + s)) break;
-        if (!mbar_wait(&a_full[sa], (it / AS) & 1, abort_flag, 0x220 + sa)) break;
-        tc_fence_after();
-        const int rows_t = min(NT_MAX, m_e - tile * NT_MAX);
-        const int nt = (rows_t + 15) & ~15;
-        const int box = 16 << box_index(rows_t);
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
+        const Item item = item_at(u);
+        const int nt = (item.rows_t + 15) & ~15;
+        const int box = 16 << box_index(item.rows_t);
         const uint32_t idesc = make_idesc(nt);
-        const uint32_t bbase = smem_u32(sb + s * C::B_STAGE_BYTES);
-        const uint32_t a_stage = a_base + sa * C::A_STAGE_COLS;
-#pragma unroll
-        for (int j = 0; j < KC / 16; ++j) {
-          const uint64_t bdesc = make_sdesc(bbase + (j >> 2) * box * 128 + (j & 3) * 32);
-          const uint32_t acc = (kc > 0 || j > 0) ? 1u : 0u;
-          tc_mma(acc_a, a_stage + j * 8, bdesc, idesc, acc);
-          if (GEMM1) tc_mma(acc_b, a_stage + KC / 2 + j * 8, bdesc, idesc, acc);
+        if (!FAST) {
+          if (!mbar_wait(&acc_empty[0], (ii & 1) ^ 1, abort_flag, 0x200)) break;
+          tc_fence_after();
         }
-        tc_commit(&a_empty[sa]);
-        tc_commit(&empty[s]);
-        if (kc == kch - 1) tc_commit(acc_full);
+        for (int kc = 0; kc < kch; ++kc, ++it) {
+          const int s = it % S, sa = it % AS;
+          uint32_t d0 = tmem, d1 = tmem + NTM;
+          if (FAST) {
+            const int pb = it & 1;
+            if (!mbar_wait(&acc_empty[pb], ((it >> 1) & 1) ^ 1, abort_flag, 0x210 + pb)) { ok = false; break; }
+            d0 = tmem + pb * 2 * NTM;
+            d1 = d0 + NTM;
+          }
+          if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, 0x220 + s)) { ok = false; break; }
+          if (!mbar_wait(&a_full[sa], (it / AS) & 1, abort_flag, 0x230 + sa)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t bbase = smem_u32(sb + s * C::B_STAGE_BYTES);
+          const uint32_t a_stage = a_base + sa * C::A_STAGE_COLS;
+#pragma unroll
+          for (int j = 0; j < KC / 16; ++j) {
+            const uint64_t bdesc = make_sdesc(bbase + (j >> 2) * box * 128 + (j & 3) * 32);
+            const uint32_t acc = FAST ? (j > 0 ? 1u : 0u) : ((kc > 0 || j > 0) ? 1u : 0u);
+            tc_mma(d0, a_stage + j * 8, bdesc, idesc, acc);
+            tc_mma(d1, a_stage + KC / 2 + j * 8, bdesc, idesc, acc);
+          }
+          tc_commit(&a_empty[sa]);
+          tc_commit(&empty[s]);
+          if (FAST) tc_commit(&acc_full[it & 1]);
+          else if (kc == kch - 1) tc_commit(&acc_full[0]);
+        }
       }
     }
-  } else {
-    // ------------------------------------------------------------- dequant + epilogue
-    const int dw = warp - 2;            // 0..7
-    const int wg = dw >> 2;             // warpgroup 0/1
-    const int q = warp & 3;             // TMEM lane quarter this warp may access
-    const int r = q * 32 + lane;        // weight row within the 128-row tile
-    const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
-    const uint32_t a_base = tmem + C::ACC_COLS + lane_addr;
-    // GEMM1: warpgroup 0 = gate rows, 1 = up rows (all chunks);
-    // GEMM2: both on the same rows, warpgroup g takes half of the chunks.
-    const int tile_sel = GEMM1 ? wg : 0;
-    const int c_begin = GEMM1 ? 0 : wg * (C::CHUNKS / 2);
-    const int c_end = GEMM1 ? C::CHUNKS : c_begin + C::CHUNKS / 2;
-    const int64_t wrow = (tile_sel == 0 ? wrow_a : wrow_b) + r;
-    const float* srow = args.scale + wrow * args.groups;
+  } else if (warp < FIRST_EPI) {
+    // ------------------------------------------------------------- dequant
+    const int wg = (warp - FIRST_DQ) >> 2;  // 0: tile 0, 1: tile 1
+    const int q = warp & 3;                 // TMEM lane quarter
+    const int r = q * 32 + lane;            // row within the tile
+    const uint32_t a_row = tmem + C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16) + wg * (KC / 2);
+    int it = 0;
     bool ok = true;
-    for (int it = 0; it < total && ok; ++it) {
-      const int tile = it / kch, kc = it - tile * kch, s = it % S, sa = it % AS;
-      if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, 0x300 + s)) { ok = false; break; }
-      if (!mbar_wait(&a_empty[sa], ((it / AS) & 1) ^ 1, abort_flag, 0x310 + sa)) { ok = false; break; }
-      tc_fence_after();
-      const float sc = srow[args.group > 0 ? (kc * KC) / args.group : 0];
-      const uint8_t* wt = sw + s * C::W_STAGE_BYTES + tile_sel * C::W_TILE_BYTES + r * C::W_ROW_BYTES;
-      const uint32_t a_stage = a_base + sa * C::A_STAGE_COLS + tile_sel * (KC / 2);
-      if (BITS == 4) {
-#pragma unroll
-        for (int c = c_begin; c < c_end; ++c) {
-          const int pc = c ^ ((r >> 1) & 3);  // 64-byte swizzle
-          const uint4 v = *reinterpret_cast<const uint4*>(wt + pc * 16);
-          uint32_t o[16];
-          dequant_int4_chunk(v, sc, o);
-          tc_st16(a_stage + c * 16, o);
-        }
-      } else {
-#pragma unroll
-        for (int c = c_begin; c < c_end; c += 2) {
-          const uint4 v0 = *reinterpret_cast<const uint4*>(wt + ((c ^ (r & 7)) * 16));
-          const uint4 v1 = *reinterpret_cast<const uint4*>(wt + (((c + 1) ^ (r & 7)) * 16));
-          uint32_t o[16];
-          dequant_int8_chunk(v0, sc, o);
-          dequant_int8_chunk(v1, sc, o + 8);
-          tc_st16(a_stage + c * 8, o);
-        }
-      }
-      tc_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&a_full[sa]);
-        mbar_arrive(&empty[s]);
-      }
-      if (kc == kch - 1) {
-        // ---- epilogue of this token tile
-        if (!mbar_wait(acc_full, tile & 1, abort_flag, 0x320)) { ok = false; break; }
+    for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
+      const int sbuf = ii & 1;
+      if (!mbar_wait(&sc_full[sbuf], (ii >> 1) & 1, abort_flag, 0x300)) break;
+      const float* srow = ssc + sbuf * (2 * ROWS * MAX_G) + wg * (ROWS * MAX_G) + r * G;
+      for (int kc = 0; kc < kch; ++kc, ++it) {
+        const int s = it % S, sa = it % AS;
+        if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, 0x310 + s)) { ok = false; break; }
+        if (!mbar_wait(&a_empty[sa], ((it / AS) & 1) ^ 1, abort_flag, 0x320 + sa)) { ok = false; break; }
         tc_fence_after();
-        const int rows_t = min(NT_MAX, m_e - tile * NT_MAX);
-        const int nt = (rows_t + 15) & ~15;
-        const int half = nt >> 1;
-        const int n_glob = rb * ROWS + r;
-        for (int t0 = wg * half; t0 < (wg + 1) * half; t0 += 8) {
-          float va[8], vb[8];
-          tc_ld8(tmem + lane_addr + t0, va);
-          if (GEMM1) tc_ld8(tmem + lane_addr + NT_MAX + t0, vb);
+        const uint8_t* wt = sw + s * C::W_STAGE_BYTES + wg * C::W_TILE_BYTES + r * C::W_ROW_BYTES;
+        const uint32_t a_stage = a_row + sa * C::A_STAGE_COLS;
+        if (BITS == 4) {
+          const float sc = FAST ? 0.f : srow[args.group > 0 ? (kc * KC) / args.group : 0];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int t = t0 + i;
-            if (t >= rows_t) break;
-            const int64_t p = static_cast<int64_t>(row0) + tile * NT_MAX + t;
-            if (GEMM1) {
-              const float g = round_bf16(va[i]);
-              const float u = round_bf16(vb[i]);
-              const float silu = round_bf16(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))));
-              args.out[p * args.n_out + n_glob] = __float2bfloat16_rn(__fmul_rn(silu, u));
-            } else {
-              const int32_t slot = args.sorted_slots[p];
-              args.out[static_cast<int64_t>(slot) * args.n_out + n_glob] =
-                  __float2bfloat16_rn(__fmul_rn(va[i], args.topk_w[slot]));
+          for (int c = 0; c < C::CHUNKS; ++c) {
+            const uint4 v = *reinterpret_cast<const uint4*>(wt + ((c ^ ((r >> 1) & 3)) * 16));
+            uint32_t o[16];
+            if (FAST) codes_int4(v, o);
+            else dequant_int4_exact(v, sc, o);
+            tc_st16(a_stage + c * 16, o);
+          }
+        } else {
+          const float sc = srow[args.group > 0 ? (kc * KC) / args.group : 0];
+#pragma unroll
+          for (int c = 0; c < C::CHUNKS; c += 2) {
+            const uint4 v0 = *reinterpret_cast<const uint4*>(wt + ((c ^ (r & 7)) * 16));
+            const uint4 v1 = *reinterpret_cast<const uint4*>(wt + (((c + 1) ^ (r & 7)) * 16));
+            uint32_t o[16];
+            dequant_int8_exact(v0, sc, o);
+            dequant_int8_exact(v1, sc, o + 8);
+            tc_st16(a_stage + c * 8, o);
+          }
+        }
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&a_full[sa]);
+          mbar_arrive(&empty[s]);
+        }
+      }
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(&sc_empty[sbuf]);
+    }
+  } else {
+    // ------------------------------------------------------------- epilogue
+    const int eg = (warp - FIRST_EPI) >> 2;  // token half
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+    constexpr int HALF = NTM / 2;
+    int it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
+      const Item item = item_at(u);
+      const int nt = (item.rows_t + 15) & ~15;
+      const int t_begin = eg * (nt / 2), t_end = (eg + 1) * (nt / 2);
+      // one token's outputs from the two fp32 accumulators of row r
+      auto emit = [&](int t, float a0, float a1) {
+        if (t >= t_end || t >= item.rows_t) return;
+        const int64_t p = static_cast<int64_t>(item.row0) + t;
+        if (GEMM1) {
+          const float g = round_bf16(a0);
+          const float up = round_bf16(a1);
+          const float silu = round_bf16(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))));
+          const int n = item.rb * ROWS + r;
+          const int pos = FAST ? kperm_pos(n) : n;
+          args.out[p * args.n_out + pos] = __float2bfloat16_rn(__fmul_rn(silu, up));
+        } else {
+          const int32_t slot = args.sorted_slots[p];
+          const float w = args.topk_w[slot];
+          __nv_bfloat16* orow = args.out + static_cast<int64_t>(slot) * args.n_out + item.rb * 2 * ROWS + r;
+          orow[0] = __float2bfloat16_rn(__fmul_rn(a0, w));
+          orow[ROWS] = __float2bfloat16_rn(__fmul_rn(a1, w));
+        }
+      };
+      if (FAST) {
+        const int sbuf = ii & 1;
+        float acc0[FAST ? HALF : 1], acc1[FAST ? HALF : 1];
+#pragma unroll
+        for (int i = 0; i < (FAST ? HALF : 1); ++i) acc0[i] = acc1[i] = 0.f;
+        if (!mbar_wait(&sc_full[sbuf], (ii >> 1) & 1, abort_flag, 0x400)) break;
+        const float* s0row = ssc + sbuf * (2 * ROWS * MAX_G) + r * G;
+        const float* s1row = s0row + ROWS * MAX_G;
+        for (int kc = 0; kc < kch; ++kc, ++it) {
+          const int pb = it & 1;
+          if (!mbar_wait(&acc_full[pb], (it >> 1) & 1, abort_flag, 0x410 + pb)) { ok = false; break; }
+          tc_fence_after();
+          const int gi = args.group > 0 ? (kc * KC) / args.group : 0;
+          const float s0 = s0row[gi], s1 = s1row[gi];
+          const uint32_t p0 = tmem + lane_addr + pb * 2 * NTM, p1 = p0 + NTM;
+#pragma unroll
+          for (int c = 0; c < HALF / 8; ++c) {
+            const int t0 = t_begin + c * 8;
+            if (t0 < t_end) {
+              float v0[8], v1[8];
+              tc_ld8(p0 + t0, v0);
+              tc_ld8(p1 + t0, v1);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                acc0[(c * 8 + i) % (FAST ? HALF : 1)] = __fmaf_rn(s0, v0[i], acc0[(c * 8 + i) % (FAST ? HALF : 1)]);
+                acc1[(c * 8 + i) % (FAST ? HALF : 1)] = __fmaf_rn(s1, v1[i], acc1[(c * 8 + i) % (FAST ? HALF : 1)]);
+              }
             }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[pb]);
+        }
+        if (!ok) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sc_empty[sbuf]);
+#pragma unroll
+        for (int i = 0; i < (FAST ? HALF : 1); ++i) emit(t_begin + i, acc0[i], acc1[i]);
+      } else {
+        if (!mbar_wait(&acc_full[0], ii & 1, abort_flag, 0x420)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < HALF / 8; ++c) {
+          const int t0 = t_begin + c * 8;
+          if (t0 < t_end) {
+            float v0[8], v1[8];
+            tc_ld8(tmem + lane_addr + t0, v0);
+            tc_ld8(tmem + lane_addr + NTM + t0, v1);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) emit(t0 + i, v0[i], v1[i]);
           }
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(acc_empty);
+        if (lane == 0) mbar_arrive(&acc_empty[0]);
       }
     }
   }
@@ -494,11 +688,11 @@ int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t 
   return LLQ_OK;
 }
 
-template <bool GEMM1, int BITS>
+template <bool GEMM1, int BITS, bool FAST, int NTM>
 int launch_tc(const void* act, int64_t n_rows, const int32_t* offsets, int E, int K, int rows_total,
               int inter, int n_out, const int8_t* q, const float* scale, int group_size,
               const int32_t* sorted_slots, const float* topk_w, void* out, cudaStream_t st) {
-  using C = Cfg<GEMM1, BITS>;
+  using C = Cfg<GEMM1, BITS, FAST, NTM>;
   if (n_rows <= 0) return LLQ_OK;
   CUtensorMap tw, tb[4];
   const uint64_t k_bytes = static_cast<uint64_t>(K) * BITS / 8;
@@ -507,8 +701,9 @@ int launch_tc(const void* act, int64_t n_rows, const int32_t* offsets, int E, in
                     BITS == 4 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   for (int i = 0; i < 4; ++i) {
+    const uint32_t box = 16u << (i < 3 || NTM >= 128 ? i : 2);
     rc = make_map(&tb[i], act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, static_cast<uint64_t>(n_rows),
-                  static_cast<uint64_t>(K) * 2, 64, 16u << i, CU_TENSOR_MAP_SWIZZLE_128B);
+                  static_cast<uint64_t>(K) * 2, 64, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
   TcArgs a;
@@ -517,58 +712,83 @@ int launch_tc(const void* act, int64_t n_rows, const int32_t* offsets, int E, in
   a.sorted_slots = sorted_slots;
   a.topk_w = topk_w;
   a.out = static_cast<__nv_bfloat16*>(out);
+  a.E = E;
   a.K = K;
   a.rows_total = rows_total;
   a.inter = inter;
   a.n_out = n_out;
+  a.rblocks = GEMM1 ? inter / ROWS : n_out / (2 * ROWS);
   const bool grouped = group_size > 0 && K % group_size == 0;
   a.group = grouped ? group_size : 0;
   a.groups = grouped ? K / group_size : 1;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(moe_gemm_tc_kernel<GEMM1, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(moe_gemm_tc_kernel<GEMM1, BITS, FAST, NTM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(C::SMEM_BYTES));
     attr = true;
   }
-  dim3 grid(n_out / ROWS, E);
-  moe_gemm_tc_kernel<GEMM1, BITS><<<grid, THREADS, C::SMEM_BYTES, st>>>(tw, tb[0], tb[1], tb[2], tb[3], a);
+  const int grid = num_sms();
+  moe_gemm_tc_kernel<GEMM1, BITS, FAST, NTM><<<grid, THREADS, C::SMEM_BYTES, st>>>(tw, tb[0], tb[1], tb[2],
+                                                                                  tb[3], a);
   return check_launch("moe_gemm_tc_kernel");
+}
+
+// decode tiles (64 tokens) unless the average expert holds more than 96 rows
+template <bool GEMM1, int BITS, bool FAST>
+int launch_any(int64_t n_rows, int E, const void* act, const int32_t* offsets, int K, int rows_total,
+               int inter, int n_out, const int8_t* q, const float* scale, int group_size,
+               const int32_t* sorted_slots, const float* topk_w, void* out, cudaStream_t st) {
+  if (!FAST && n_rows > static_cast<int64_t>(E) * 96)
+    return launch_tc<GEMM1, BITS, false, 128>(act, n_rows, offsets, E, K, rows_total, inter, n_out, q, scale,
+                                              group_size, sorted_slots, topk_w, out, st);
+  return launch_tc<GEMM1, BITS, FAST, 64>(act, n_rows, offsets, E, K, rows_total, inter, n_out, q, scale,
+                                          group_size, sorted_slots, topk_w, out, st);
 }
 
 }  // namespace
 
 bool tc_supported(int E, int N_out, int K, int bits, int group_size, bool gemm1) {
-  (void)gemm1;
   if (bits != 4 && bits != 8) return false;
-  if (E < 1 || E > 65535) return false;
-  if (K % KC != 0 || N_out % ROWS != 0) return false;
+  if (E < 1 || E > MAX_E) return false;
+  if (K % KC != 0 || K > KC * MAX_G) return false;
+  if (N_out % (gemm1 ? ROWS : 2 * ROWS) != 0) return false;
   const bool grouped = group_size > 0 && K % group_size == 0;
   if (grouped && group_size % KC != 0) return false;  // one scale per 128-element step
   return true;
 }
 
 int gemm1_tc(const void* x_sorted, const int32_t* offsets, int64_t n_rows, int E, int H, int I,
-             const int8_t* qw1, const float* sw1, int bits, int group_size, void* h_sorted,
+             const int8_t* qw1, const float* sw1, int bits, int group_size, void* h_sorted, bool fast,
              cudaStream_t st) {
   if (!tc_supported(E, I, H, bits, group_size, true))
     return fail(LLQ_EUNSUPPORTED, "tcgen05 GEMM1: unsupported shape");
-  if (bits == 4)
-    return launch_tc<true, 4>(x_sorted, n_rows, offsets, E, H, 2 * I, I, I, qw1, sw1, group_size, nullptr,
-                              nullptr, h_sorted, st);
-  return launch_tc<true, 8>(x_sorted, n_rows, offsets, E, H, 2 * I, I, I, qw1, sw1, group_size, nullptr,
-                            nullptr, h_sorted, st);
+  if (fast && bits != 4) return fail(LLQ_EUNSUPPORTED, "fast dequantization is INT4 only");
+  if (bits == 4) {
+    if (fast)
+      return launch_any<true, 4, true>(n_rows, E, x_sorted, offsets, H, 2 * I, I, I, qw1, sw1, group_size,
+                                       nullptr, nullptr, h_sorted, st);
+    return launch_any<true, 4, false>(n_rows, E, x_sorted, offsets, H, 2 * I, I, I, qw1, sw1, group_size,
+                                      nullptr, nullptr, h_sorted, st);
+  }
+  return launch_any<true, 8, false>(n_rows, E, x_sorted, offsets, H, 2 * I, I, I, qw1, sw1, group_size,
+                                    nullptr, nullptr, h_sorted, st);
 }
 
 int gemm2_tc(const void* h_sorted, const int32_t* offsets, const int32_t* sorted_slots,
              const float* topk_w, int64_t n_rows, int E, int H, int I, const int8_t* qw2,
-             const float* sw2, int bits, int group_size, void* y_slots, cudaStream_t st) {
+             const float* sw2, int bits, int group_size, void* y_slots, bool fast, cudaStream_t st) {
   if (!tc_supported(E, H, I, bits, group_size, false))
     return fail(LLQ_EUNSUPPORTED, "tcgen05 GEMM2: unsupported shape");
-  if (bits == 4)
-    return launch_tc<false, 4>(h_sorted, n_rows, offsets, E, I, H, 0, H, qw2, sw2, group_size,
-                               sorted_slots, topk_w, y_slots, st);
-  return launch_tc<false, 8>(h_sorted, n_rows, offsets, E, I, H, 0, H, qw2, sw2, group_size,
-                             sorted_slots, topk_w, y_slots, st);
+  if (fast && bits != 4) return fail(LLQ_EUNSUPPORTED, "fast dequantization is INT4 only");
+  if (bits == 4) {
+    if (fast)
+      return launch_any<false, 4, true>(n_rows, E, h_sorted, offsets, I, H, 0, H, qw2, sw2, group_size,
+                                        sorted_slots, topk_w, y_slots, st);
+    return launch_any<false, 4, false>(n_rows, E, h_sorted, offsets, I, H, 0, H, qw2, sw2, group_size,
+                                       sorted_slots, topk_w, y_slots, st);
+  }
+  return launch_any<false, 8, false>(n_rows, E, h_sorted, offsets, I, H, 0, H, qw2, sw2, group_size,
+                                     sorted_slots, topk_w, y_slots, st);
 }
 
 }  // namespace llq

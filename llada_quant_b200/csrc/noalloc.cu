@@ -28,7 +28,7 @@ namespace llq {
 
 int align_impl(const int32_t*, int64_t, int, int, int32_t*, int32_t*, void*, size_t, cudaStream_t);
 size_t align_workspace_size(int64_t, int, int);
-int permute_impl(const void*, int64_t, int, int, const int32_t*, void*, cudaStream_t);
+int permute_impl(const void*, int64_t, int, int, const int32_t*, void*, cudaStream_t, int);
 int combine_impl(const void*, int64_t, int, int, void*, cudaStream_t);
 
 namespace {
@@ -109,7 +109,7 @@ int llq_fused_moe_packed_noalloc(const void* x, const int8_t* qw1, const float* 
   cudaStream_t st = as_stream(stream);
   rc = align_impl(topk_ids, T, k, E, offsets, slots, align_ws, kAlignBytes, st);
   if (rc) return rc;
-  rc = permute_impl(x, T, H, k, slots, acts, st);
+  rc = permute_impl(x, T, H, k, slots, acts, st, 0);
   if (rc) return rc;
   rc = llq_moe_gemm1(acts, offsets, rows, E, H, I, qw1, sw1, bits, group_size, inter, impl, stream);
   if (rc) return rc;

@@ -268,6 +268,9 @@ __global__ void __launch_bounds__(kAlignThreads) align_scatter_kernel(
   }
 }
 
+// kperm: reorder each 8-element block as [0,4,1,5,2,6,3,7], the K order in
+// which the fast-mode expert GEMM lays out its integer weight codes
+template <bool KPERM>
 __global__ void permute_kernel(const uint4* __restrict__ x, int64_t n_rows, int vec_per_row, int k,
                                const int32_t* __restrict__ sorted_slots, uint4* __restrict__ xs) {
   const int64_t total = n_rows * vec_per_row;
@@ -276,7 +279,15 @@ __global__ void permute_kernel(const uint4* __restrict__ x, int64_t n_rows, int 
     const int64_t p = i / vec_per_row;
     const int v = static_cast<int>(i - p * vec_per_row);
     const int64_t tok = sorted_slots[p] / k;
-    xs[i] = __ldg(x + tok * vec_per_row + v);
+    uint4 val = __ldg(x + tok * vec_per_row + v);
+    if (KPERM) {
+      const uint4 in = val;
+      val.x = __byte_perm(in.x, in.z, 0x5410);
+      val.y = __byte_perm(in.x, in.z, 0x7632);
+      val.z = __byte_perm(in.y, in.w, 0x5410);
+      val.w = __byte_perm(in.y, in.w, 0x7632);
+    }
+    xs[i] = val;
   }
 }
 
@@ -381,13 +392,17 @@ int align_impl(const int32_t* ids, int64_t T, int k, int E, int32_t* offsets, in
 }
 
 int permute_impl(const void* x, int64_t T, int H, int k, const int32_t* sorted_slots, void* xs,
-                 cudaStream_t st) {
+                 cudaStream_t st, int kperm) {
   if (H % 8 != 0) return fail(LLQ_EUNSUPPORTED, "hidden size must be a multiple of 8");
   const int64_t n = T * k;
   if (n == 0) return LLQ_OK;
   const int vpr = H / 8;
-  permute_kernel<<<grid_for(n * vpr, 256), 256, 0, st>>>(static_cast<const uint4*>(x), n, vpr, k,
-                                                         sorted_slots, static_cast<uint4*>(xs));
+  if (kperm)
+    permute_kernel<true><<<grid_for(n * vpr, 256), 256, 0, st>>>(static_cast<const uint4*>(x), n, vpr, k,
+                                                                 sorted_slots, static_cast<uint4*>(xs));
+  else
+    permute_kernel<false><<<grid_for(n * vpr, 256), 256, 0, st>>>(static_cast<const uint4*>(x), n, vpr, k,
+                                                                  sorted_slots, static_cast<uint4*>(xs));
   return check_launch("permute_kernel");
 }
 

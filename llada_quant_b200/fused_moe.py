@@ -26,7 +26,8 @@ import torch
 from . import _lib, ops
 from .moe import PackedExperts
 
-IMPL = {"auto": _lib.LLQ_GEMM_AUTO, "tcgen05": _lib.LLQ_GEMM_TCGEN05, "simt": _lib.LLQ_GEMM_SIMT}
+IMPL = {"auto": _lib.LLQ_GEMM_AUTO, "tcgen05": _lib.LLQ_GEMM_TCGEN05, "simt": _lib.LLQ_GEMM_SIMT,
+        "tcgen05_fast": _lib.LLQ_GEMM_TCGEN05_FAST}
 
 
 def routing_weights(gating_output: torch.Tensor, topk_ids: torch.Tensor,

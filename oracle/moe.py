@@ -149,6 +149,45 @@ def fused_moe_packed(x: np.ndarray, qw1, sw1, qw2, sw2, topk_w: np.ndarray, topk
     return out
 
 
+def fused_moe_f64(x: np.ndarray, qw1, sw1, qw2, sw2, topk_w: np.ndarray, topk_ids: np.ndarray,
+                  bits: int) -> np.ndarray:
+    """The quantized layer's exact mathematics: W = q * s in float64, no intermediate
+    rounding at all.  Neither the reference path nor any kernel computes this; it is
+    the yardstick both are measured against."""
+    from .symmetric import unpack_int4
+    packed = bits == 4
+
+    def deq64(q, s):
+        qq = unpack_int4(q) if packed else q
+        K = qq.shape[-1]
+        G = s.shape[-1]
+        if G <= 1:
+            return qq.astype(np.float64) * s.astype(np.float64)
+        g = K // G
+        return (qq.astype(np.float64).reshape(*qq.shape[:-1], G, g)
+                * s.astype(np.float64)[..., None]).reshape(qq.shape)
+
+    w1 = deq64(qw1, sw1)
+    w2 = deq64(qw2, sw2)
+    inter = w2.shape[-1]
+    T, H = x.shape
+    out = np.zeros((T, H), dtype=np.float64)
+    offsets, slots = moe_align(topk_ids, qw1.shape[0])
+    k = topk_ids.shape[1]
+    flat_w = topk_w.reshape(-1).astype(np.float64)
+    for e in range(qw1.shape[0]):
+        lo, hi = int(offsets[e]), int(offsets[e + 1])
+        if lo == hi:
+            continue
+        sl = slots[lo:hi].astype(np.int64)
+        a = x[sl // k].astype(np.float64) @ w1[e].T
+        g, u = a[:, :inter], a[:, inter:]
+        h = g / (1.0 + np.exp(-g)) * u
+        y = (h @ w2[e].T) * flat_w[sl][:, None]
+        np.add.at(out, sl // k, y)
+    return out
+
+
 def moe_layer(x: np.ndarray, gate_w: np.ndarray, qw1, sw1, qw2, sw2, k: int, bits: int,
               bias=None, renormalize: bool = False, weights=None):
     """Full layer: router + routed experts.  Returns ``(out, topk_w, topk_ids, logits)``."""

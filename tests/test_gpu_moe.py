@@ -24,7 +24,7 @@ from tests._util import random_routing, synthetic_layer, synthetic_tokens, to_np
 
 pytestmark = pytest.mark.gpu
 
-IMPLS = ["simt", "tcgen05"]
+IMPLS = ["simt", "tcgen05", "tcgen05_fast"]
 
 
 @pytest.fixture(autouse=True)
@@ -37,8 +37,12 @@ def _no_device_timeouts():
     assert ops.device_error() == 0, f"device error word {ops.device_error():#x}"
 
 
-def _impl_or_skip(impl):
+def _impl_or_skip(impl, bits=4):
     from llada_quant_b200 import _lib
+    if impl == "tcgen05_fast":
+        if bits != 4:
+            pytest.skip("the fast (scale-after-MMA) mode is INT4 only")
+        return _lib.LLQ_GEMM_TCGEN05_FAST
     if impl == "tcgen05":
         return _lib.LLQ_GEMM_TCGEN05
     return _lib.LLQ_GEMM_SIMT
@@ -52,9 +56,19 @@ def _quantize(E, H, I, bits, search="amax", seed=0):
     return r1, r2
 
 
-def _assert_layer_close(out, ref):
+def _assert_layer_close(out, ref, fast=False, truth=None):
+    """Exact-weight modes: rel-L2 <= 3e-3 and max-abs <= 2 bf16 ulps of the largest output.
+    Fast mode (W = q*s without bf16 weight rounding): rel-L2 <= 1e-2 against the oracle,
+    and -- when the fp64 evaluation of the quantized layer is given -- no further from it
+    than the oracle (the reference path) itself is, with 10% slack."""
     rel = M.rel_l2(out, ref)
     mx = M.max_abs(out, ref)
+    if fast:
+        assert rel <= 1e-2, rel
+        if truth is not None:
+            assert M.rel_l2(out, truth) <= 1.1 * M.rel_l2(ref, truth) + 1e-6, (
+                M.rel_l2(out, truth), M.rel_l2(ref, truth))
+        return rel, mx
     bound = 2 * 2.0 ** -7 * max(np.abs(ref).max(), 1e-6)
     assert rel <= 3e-3, rel
     assert mx <= bound, (mx, bound)
@@ -63,18 +77,16 @@ def _assert_layer_close(out, ref):
 
 def _run_layer(T, E, H, I, k, bits, impl, skew=None, search="amax", seed=0):
     from llada_quant_b200 import ops
+    code = _impl_or_skip(impl, bits)
     r1, r2 = _quantize(E, H, I, bits, search, seed)
     x = synthetic_tokens(T, H)
     tw, ids = random_routing(T, E, k, seed=seed + T, skew=skew)
-    try:
-        out = ops.fused_moe_packed(x.cuda(), r1.q, r1.scale, r2.q, r2.scale,
-                                   torch.from_numpy(tw).cuda(), torch.from_numpy(ids).cuda(), bits,
-                                   _impl_or_skip(impl))
-    except Exception as e:  # tcgen05 may decline a shape: that is a failure for supported shapes
-        raise
-    ref = M.fused_moe_packed(to_np(x), to_np(r1.q), to_np(r1.scale), to_np(r2.q), to_np(r2.scale),
-                             tw, ids, bits)
-    return to_np(out), ref
+    out = ops.fused_moe_packed(x.cuda(), r1.q, r1.scale, r2.q, r2.scale,
+                               torch.from_numpy(tw).cuda(), torch.from_numpy(ids).cuda(), bits, code)
+    args = (to_np(x), to_np(r1.q), to_np(r1.scale), to_np(r2.q), to_np(r2.scale), tw, ids, bits)
+    ref = M.fused_moe_packed(*args)
+    truth = M.fused_moe_f64(*args) if impl == "tcgen05_fast" else None
+    return to_np(out), ref, truth
 
 
 @pytest.mark.parametrize("impl", IMPLS)
@@ -87,21 +99,21 @@ def _run_layer(T, E, H, I, k, bits, impl, skew=None, search="amax", seed=0):
     (7, 16, 1024, 512, 2, 8),
 ])
 def test_fused_layer_matches_oracle(impl, T, E, H, I, k, bits):
-    out, ref = _run_layer(T, E, H, I, k, bits, impl)
-    _assert_layer_close(out, ref)
+    out, ref, truth = _run_layer(T, E, H, I, k, bits, impl)
+    _assert_layer_close(out, ref, impl == "tcgen05_fast", truth)
 
 
 @pytest.mark.parametrize("impl", IMPLS)
 def test_skewed_routing_one_hot_expert(impl):
     """Zipf-skewed routing: one expert gets most tokens (> one token tile)."""
-    out, ref = _run_layer(600, 16, 1024, 512, 2, 4, impl, skew=3.0)
-    _assert_layer_close(out, ref)
+    out, ref, truth = _run_layer(600, 16, 1024, 512, 2, 4, impl, skew=3.0)
+    _assert_layer_close(out, ref, impl == "tcgen05_fast", truth)
 
 
 @pytest.mark.parametrize("impl", IMPLS)
 def test_mse_weights(impl):
-    out, ref = _run_layer(128, 16, 1024, 512, 2, 4, impl, search="mse")
-    _assert_layer_close(out, ref)
+    out, ref, truth = _run_layer(128, 16, 1024, 512, 2, 4, impl, search="mse")
+    _assert_layer_close(out, ref, impl == "tcgen05_fast", truth)
 
 
 @pytest.mark.parametrize("impl", IMPLS)
@@ -113,13 +125,18 @@ def test_layer_vs_reference_golden(golden, impl, name):
     bits = int(golden[f"{name}/bits"])
     x = torch.from_numpy(S.from_bf16_bits(golden["moe/x"])).to(torch.bfloat16).cuda()
     t = lambda a: torch.from_numpy(golden[a]).cuda()
+    code = _impl_or_skip(impl, bits)
     out = ops.fused_moe_packed(x, t(f"{name}/qw1"), t(f"{name}/sw1"), t(f"{name}/qw2"),
-                               t(f"{name}/sw2"), t("moe/topk_w"), t("moe/topk_ids"), bits,
-                               _impl_or_skip(impl))
-    _assert_layer_close(to_np(out), S.from_bf16_bits(golden[f"{name}/out"]))
+                               t(f"{name}/sw2"), t("moe/topk_w"), t("moe/topk_ids"), bits, code)
+    truth = None
+    if impl == "tcgen05_fast":
+        truth = M.fused_moe_f64(S.from_bf16_bits(golden["moe/x"]), golden[f"{name}/qw1"],
+                                golden[f"{name}/sw1"], golden[f"{name}/qw2"], golden[f"{name}/sw2"],
+                                golden["moe/topk_w"], golden["moe/topk_ids"], bits)
+    _assert_layer_close(to_np(out), S.from_bf16_bits(golden[f"{name}/out"]), impl == "tcgen05_fast", truth)
 
 
-@pytest.mark.parametrize("impl", IMPLS)
+@pytest.mark.parametrize("impl", ["simt", "tcgen05"])
 def test_gemm_stages_match_oracle(impl):
     """GEMM1 (SiLU epilogue) and GEMM2 (routed weight, scatter) separately."""
     from llada_quant_b200 import ops
