@@ -307,7 +307,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         for l in range(N_LAYERS):
             tw, ids, _ = ops.route(xs[l], gate_w, TOPK, None, False)
             offsets, slots = ops.moe_align(ids, E)
-            xsrt = ops.moe_permute(xs[l], slots, TOPK)
+            xsrt = ops.moe_permute(xs[l], slots, TOPK, args.gemm == "tcgen05_fast")
             hit = int((offsets[1:] - offsets[:-1] > 0).sum().item())
             preps.append((xsrt, offsets, hit))
         for l in range(N_LAYERS):
@@ -376,7 +376,7 @@ def kernel_case(args):
     for _ in range(2):
         tw, ids, _ = ops.route(x, gate_w, TOPK, None, False)
         off, slots = ops.moe_align(ids, E)
-        xs = ops.moe_permute(x, slots, TOPK)
+        xs = ops.moe_permute(x, slots, TOPK, args.gemm == "tcgen05_fast")
         h = ops.moe_gemm1(xs, off, lay.qw1, lay.sw1, BITS, impl)
         y = ops.moe_gemm2(h, off, slots, tw, lay.qw2, lay.sw2, BITS, impl)
         out = ops.moe_combine(y, TOPK)

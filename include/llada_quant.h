@@ -134,9 +134,13 @@ size_t llq_align_workspace_size(int64_t T, int k, int E);
 int llq_moe_align(const int32_t* topk_ids, int64_t T, int k, int E, int32_t* expert_offsets,
                   int32_t* sorted_slots, void* workspace, size_t workspace_bytes, void* stream);
 
-/* Permute: x_sorted[p] = x[sorted_slots[p] / k], bf16 rows of H. */
+/*
+ * Permute: x_sorted[p] = x[sorted_slots[p] / k], bf16 rows of H.  kperm != 0
+ * also reorders each 8-element block as [0,4,1,5,2,6,3,7], the K order that the
+ * LLQ_GEMM_TCGEN05_FAST GEMMs expect (GEMM1 in that mode writes h already so).
+ */
 int llq_moe_permute(const void* x, int64_t T, int H, int k, const int32_t* sorted_slots,
-                    void* x_sorted, void* stream);
+                    int kperm, void* x_sorted, void* stream);
 
 /* Unpermute/combine: out[t] = bf16(sum_j y_slots[t*k + j]) in fp32, slot order. */
 int llq_moe_combine(const void* y_slots, int64_t T, int k, int H, void* out, void* stream);
@@ -154,6 +158,8 @@ int llq_moe_combine(const void* y_slots, int64_t T, int k, int H, void* out, voi
  *   h_sorted[p, n] = bf16(bf16(silu(gate)) * up)
  * with W1 = bf16(q * scale) exactly as dequantize_tensor.
  * qw1 int8 [E, 2I, H/2 or H], sw1 float32 [E, 2I, H/group].
+ * With impl LLQ_GEMM_TCGEN05_FAST, x_sorted must come from llq_moe_permute
+ * with kperm != 0, and h_sorted is written in that K order for GEMM2.
  */
 int llq_moe_gemm1(const void* x_sorted, const int32_t* expert_offsets, int64_t n_rows, int E,
                   int H, int I, const int8_t* qw1, const float* sw1, int bits, int group_size,

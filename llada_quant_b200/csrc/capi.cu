@@ -153,9 +153,9 @@ int llq_moe_align(const int32_t* topk_ids, int64_t T, int k, int E, int32_t* exp
                     as_stream(stream));
 }
 
-int llq_moe_permute(const void* x, int64_t T, int H, int k, const int32_t* sorted_slots, void* x_sorted,
-                    void* stream) {
-  return permute_impl(x, T, H, k, sorted_slots, x_sorted, as_stream(stream), 0);
+int llq_moe_permute(const void* x, int64_t T, int H, int k, const int32_t* sorted_slots, int kperm,
+                    void* x_sorted, void* stream) {
+  return permute_impl(x, T, H, k, sorted_slots, x_sorted, as_stream(stream), kperm);
 }
 
 int llq_moe_combine(const void* y_slots, int64_t T, int k, int H, void* out, void* stream) {
@@ -165,13 +165,11 @@ int llq_moe_combine(const void* y_slots, int64_t T, int k, int H, void* out, voi
 int llq_moe_gemm1(const void* x_sorted, const int32_t* expert_offsets, int64_t n_rows, int E, int H,
                   int I, const int8_t* qw1, const float* sw1, int bits, int group_size,
                   void* h_sorted, int impl, void* stream) {
-  if (impl == LLQ_GEMM_TCGEN05_FAST)
-    return fail(LLQ_EUNSUPPORTED, "LLQ_GEMM_TCGEN05_FAST needs K-permuted activations: use llq_fused_moe_packed");
   const int which = pick_impl(impl, E, I, H, bits, group_size, true);
   if (which < 0) return fail(LLQ_EUNSUPPORTED, "tcgen05 GEMM1 does not cover this shape");
-  if (which == LLQ_GEMM_TCGEN05)
+  if (which == LLQ_GEMM_TCGEN05 || which == LLQ_GEMM_TCGEN05_FAST)
     return gemm1_tc(x_sorted, expert_offsets, n_rows, E, H, I, qw1, sw1, bits, group_size,
-                    h_sorted, false, as_stream(stream));
+                    h_sorted, which == LLQ_GEMM_TCGEN05_FAST, as_stream(stream));
   return gemm1_simt(x_sorted, expert_offsets, E, H, I, qw1, sw1, bits, group_size, h_sorted,
                     as_stream(stream));
 }
@@ -179,13 +177,11 @@ int llq_moe_gemm1(const void* x_sorted, const int32_t* expert_offsets, int64_t n
 int llq_moe_gemm2(const void* h_sorted, const int32_t* expert_offsets, const int32_t* sorted_slots,
                   const float* topk_w, int64_t n_rows, int E, int H, int I, const int8_t* qw2,
                   const float* sw2, int bits, int group_size, void* y_slots, int impl, void* stream) {
-  if (impl == LLQ_GEMM_TCGEN05_FAST)
-    return fail(LLQ_EUNSUPPORTED, "LLQ_GEMM_TCGEN05_FAST needs K-permuted activations: use llq_fused_moe_packed");
   const int which = pick_impl(impl, E, H, I, bits, group_size, false);
   if (which < 0) return fail(LLQ_EUNSUPPORTED, "tcgen05 GEMM2 does not cover this shape");
-  if (which == LLQ_GEMM_TCGEN05)
+  if (which == LLQ_GEMM_TCGEN05 || which == LLQ_GEMM_TCGEN05_FAST)
     return gemm2_tc(h_sorted, expert_offsets, sorted_slots, topk_w, n_rows, E, H, I, qw2, sw2,
-                    bits, group_size, y_slots, false, as_stream(stream));
+                    bits, group_size, y_slots, which == LLQ_GEMM_TCGEN05_FAST, as_stream(stream));
   return gemm2_simt(h_sorted, expert_offsets, sorted_slots, topk_w, E, H, I, qw2, sw2, bits,
                     group_size, y_slots, as_stream(stream));
 }

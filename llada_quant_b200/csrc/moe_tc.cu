@@ -32,6 +32,7 @@
 // No TMA multicast is used.  Every mbarrier wait is bounded (~2 s of SM
 // clocks); on timeout the kernel records a code in g_device_error, drains its
 // copies (bounded), frees TMEM and exits.
+#include <cstdlib>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -43,15 +44,26 @@ namespace {
 
 constexpr int KC = 128;
 constexpr int ROWS = 128;
-constexpr int DQ_WARPS = 8;
 constexpr int EPI_WARPS = 8;
-constexpr int FIRST_DQ = 2;
-constexpr int FIRST_EPI = FIRST_DQ + DQ_WARPS;
-constexpr int THREADS = (FIRST_EPI + EPI_WARPS) * 32;  // 576
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int MAX_G = 16;  // scale groups per row (K <= 2048 at group 128)
 constexpr int MAX_E = 256;
 constexpr long long kTimeoutCycles = 4000000000LL;
+
+// Development timeline (built only with -DLLQ_TRACE): clock64 of each role's
+// progress through the first 64 K-steps of CTA 0.
+#ifdef LLQ_TRACE
+__device__ long long g_tc_trace[8][64];
+#define LLQ_TRACE_AT(role, step)                                              \
+  do {                                                                        \
+    if (blockIdx.x == 0 && (threadIdx.x & 31) == 0 && (step) < 64)           \
+      g_tc_trace[(role)][(step)] = clock64();                                 \
+  } while (0)
+#else
+#define LLQ_TRACE_AT(role, step) \
+  do {                           \
+  } while (0)
+#endif
 
 template <bool GEMM1, int BITS, bool FAST, int NTM>
 struct Cfg {
@@ -62,8 +74,23 @@ struct Cfg {
   static constexpr int STAGE_BYTES = W_STAGE_BYTES + B_STAGE_BYTES;
   static constexpr int SCALE_BUF_BYTES = 2 * ROWS * MAX_G * 4;
   static constexpr int STAGES_FIT = (220 * 1024 - 2 * SCALE_BUF_BYTES) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_FIT > 4 ? 4 : STAGES_FIT;
-  static constexpr int ACC_COLS = FAST ? 4 * NTM : 2 * NTM;
+  static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
+  // Warp roles.  A warp issues one tcgen05.mma per ~55 cycles whatever N is,
+  // while a 128 x N x 16 MMA with N <= 64 runs in 16-32 cycles, so small-N
+  // tiles are fed by several issuing warps: one per weight tile, optionally
+  // one per (tile, even/odd 16-wide K slice) with its own accumulator (the
+  // epilogue then adds the two halves).
+  // (measured on B200 at C3: splitting K across four issuers with 16 dequant
+  // warps gained nothing over two issuers with 8 -- exact dequantization is
+  // then ALU-bound -- so SPLIT stays 1; the code keeps both layouts correct)
+  static constexpr int SPLIT = 1;
+  static constexpr int MMA_WARPS = 2 * SPLIT;
+  static constexpr int DQ_WARPS = 8;
+  static constexpr int DQ_PARTS = DQ_WARPS / 8;  // warpgroups per weight tile
+  static constexpr int FIRST_DQ = 1 + MMA_WARPS;
+  static constexpr int FIRST_EPI = FIRST_DQ + DQ_WARPS;
+  static constexpr int THREADS = (FIRST_EPI + EPI_WARPS) * 32;
+  static constexpr int ACC_COLS = FAST ? 4 * NTM : 2 * SPLIT * NTM;
   static constexpr int A_STAGE_COLS = KC;  // 64 columns per tile
   static constexpr int A_STAGES_FIT = static_cast<int>(TMEM_COLS - ACC_COLS) / A_STAGE_COLS;
   static constexpr int A_STAGES = A_STAGES_FIT > 4 ? 4 : A_STAGES_FIT;
@@ -88,6 +115,8 @@ struct TcArgs {
   int rblocks;     // 256-row blocks per expert (I/128 for GEMM1, H/256 for GEMM2)
   int group;       // 0 = one scale per row
   int groups;      // scales per row
+  int debug;       // development switch: 1 = no dequant math, 2 = no MMA, 4 = no TMEM stores,
+                   // 8 = no token-tile loads (results are wrong)
 };
 
 // ---------------------------------------------------------------------------
@@ -129,6 +158,27 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile
   if (mbar_try_wait(b, parity)) return true;
   const long long t0 = clock64();
   while (true) {
+    if (mbar_try_wait(b, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kTimeoutCycles) {
+      *abort_flag = 1;
+      atomicExch(&g_device_error, code);
+      return false;
+    }
+  }
+}
+
+// Same, for waits off the critical path (producer slots, epilogue hand-offs):
+// backs off with nanosleep so that a waiting warp does not take issue slots
+// from the dequantizing warps on its SM sub-partition.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* b, uint32_t parity, volatile int* abort_flag,
+                                                int code) {
+  if (mbar_try_wait(b, parity)) return true;
+  const long long t0 = clock64();
+  unsigned ns = 32;
+  while (true) {
+    __nanosleep(ns);
+    if (ns < 256) ns <<= 1;
     if (mbar_try_wait(b, parity)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > kTimeoutCycles) {
@@ -309,24 +359,29 @@ struct Item {
 // the kernel
 // ---------------------------------------------------------------------------
 template <bool GEMM1, int BITS, bool FAST, int NTM>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     moe_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_b0,
                        const __grid_constant__ CUtensorMap tm_b1, const __grid_constant__ CUtensorMap tm_b2,
                        const __grid_constant__ CUtensorMap tm_b3, const TcArgs args) {
   using C = Cfg<GEMM1, BITS, FAST, NTM>;
   constexpr int S = C::STAGES;
   constexpr int AS = C::A_STAGES;
+  constexpr int SPLIT = C::SPLIT;
+  constexpr int MMA_WARPS = C::MMA_WARPS;
+  constexpr int DQ_WARPS = C::DQ_WARPS;
+  constexpr int FIRST_DQ = C::FIRST_DQ;
+  constexpr int FIRST_EPI = C::FIRST_EPI;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sw = smem;
   uint8_t* sb = sw + S * C::W_STAGE_BYTES;
   float* ssc = reinterpret_cast<float*>(sb + S * C::B_STAGE_BYTES);  // [2 bufs][2 tiles][128 * G]
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(ssc) + 2 * C::SCALE_BUF_BYTES);
-  uint64_t* full = bars;
-  uint64_t* empty = full + S;
-  uint64_t* a_full = empty + S;
-  uint64_t* a_empty = a_full + AS;
-  uint64_t* sc_full = a_empty + AS;     // [2]
+  uint64_t* full = bars;                // TMA data landed
+  uint64_t* wfree = full + S;           // dequant warps have read the weight tiles
+  uint64_t* mdone = wfree + S;          // the step's MMAs completed (one commit per step)
+  uint64_t* a_full = mdone + S;         // [2 tiles][AS]: TMEM A stage written
+  uint64_t* sc_full = a_full + 2 * AS;  // [2]
   uint64_t* sc_empty = sc_full + 2;     // [2]
   uint64_t* acc_full = sc_empty + 2;    // [2] (exact uses [0])
   uint64_t* acc_empty = acc_full + 2;   // [2]
@@ -372,16 +427,14 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 32) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], DQ_WARPS + 1);
+      mbar_init(&wfree[i], DQ_WARPS);
+      mbar_init(&mdone[i], MMA_WARPS);
     }
-    for (int i = 0; i < AS; ++i) {
-      mbar_init(&a_full[i], DQ_WARPS);
-      mbar_init(&a_empty[i], 1);
-    }
+    for (int i = 0; i < 2 * AS; ++i) mbar_init(&a_full[i], DQ_WARPS / 2);  // per tile
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sc_full[i], 1);
       mbar_init(&sc_empty[i], FAST ? DQ_WARPS + EPI_WARPS : DQ_WARPS);
-      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_full[i], MMA_WARPS);
       mbar_init(&acc_empty[i], EPI_WARPS);
     }
     *abort_flag = 0;
@@ -433,7 +486,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
         const Item item = item_at(u);
         const int sbuf = ii & 1;
-        if (!mbar_wait(&sc_empty[sbuf], ((ii >> 1) & 1) ^ 1, abort_flag, 0x100)) break;
+        if (!mbar_wait_sleep(&sc_empty[sbuf], ((ii >> 1) & 1) ^ 1, abort_flag, 0x100)) break;
         const uint32_t sbytes = static_cast<uint32_t>(ROWS * G * 4);
         mbar_expect_tx(&sc_full[sbuf], 2 * sbytes);
         float* sdst = ssc + sbuf * (2 * ROWS * MAX_G);
@@ -445,14 +498,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int w0 = static_cast<int>(wrow_of(item, 0)), w1 = static_cast<int>(wrow_of(item, 1));
         for (int kc = 0; kc < kch; ++kc, ++it) {
           const int s = it % S;
-          if (!mbar_wait(&empty[s], ((it / S) & 1) ^ 1, abort_flag, 0x110 + s)) { ok = false; break; }
-          mbar_expect_tx(&full[s], C::W_STAGE_BYTES + 2 * box * 128);
+          if (!mbar_wait_sleep(&wfree[s], ((it / S) & 1) ^ 1, abort_flag, 0x110 + s)) { ok = false; break; }
+          if (!mbar_wait_sleep(&mdone[s], ((it / S) & 1) ^ 1, abort_flag, 0x118 + s)) { ok = false; break; }
+          mbar_expect_tx(&full[s], C::W_STAGE_BYTES + ((args.debug & 8) ? 0 : 2 * box * 128));
+          LLQ_TRACE_AT(0, it);
           uint8_t* wdst = sw + s * C::W_STAGE_BYTES;
           tma_load_2d(wdst, &tm_w, kc * C::W_ROW_BYTES, w0, &full[s]);
           tma_load_2d(wdst + C::W_TILE_BYTES, &tm_w, kc * C::W_ROW_BYTES, w1, &full[s]);
           uint8_t* bdst = sb + s * C::B_STAGE_BYTES;
-          tma_load_2d(bdst, tb, kc * KC, item.row0, &full[s]);
-          tma_load_2d(bdst + box * 128, tb, kc * KC + 64, item.row0, &full[s]);
+          if (!(args.debug & 8)) {
+            tma_load_2d(bdst, tb, kc * KC, item.row0, &full[s]);
+            tma_load_2d(bdst + box * 128, tb, kc * KC + 64, item.row0, &full[s]);
+          }
           ++issued;
         }
       }
@@ -463,8 +520,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------- MMA issuer
+  } else if (warp < FIRST_DQ) {
+    // ------------------------------------------------------------- MMA issuers
+    const int tile = (warp - 1) & 1;      // weight tile
+    const int par = (warp - 1) >> 1;      // K-slice parity (SPLIT == 2)
     if (lane == 0) {
       const uint32_t a_base = tmem + C::ACC_COLS;
       int it = 0;
@@ -475,12 +534,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int box = 16 << box_index(item.rows_t);
         const uint32_t idesc = make_idesc(nt);
         if (!FAST) {
-          if (!mbar_wait(&acc_empty[0], (ii & 1) ^ 1, abort_flag, 0x200)) break;
+          if (!mbar_wait_sleep(&acc_empty[0], (ii & 1) ^ 1, abort_flag, 0x200)) break;
           tc_fence_after();
         }
         for (int kc = 0; kc < kch; ++kc, ++it) {
           const int s = it % S, sa = it % AS;
-          uint32_t d0 = tmem, d1 = tmem + NTM;
+          uint32_t d0 = tmem + par * NTM, d1 = tmem + (SPLIT + par) * NTM;
           if (FAST) {
             const int pb = it & 1;
             if (!mbar_wait(&acc_empty[pb], ((it >> 1) & 1) ^ 1, abort_flag, 0x210 + pb)) { ok = false; break; }
@@ -488,27 +547,35 @@ __global__ void __launch_bounds__(THREADS, 1)
             d1 = d0 + NTM;
           }
           if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, 0x220 + s)) { ok = false; break; }
-          if (!mbar_wait(&a_full[sa], (it / AS) & 1, abort_flag, 0x230 + sa)) { ok = false; break; }
+          if (tile == 0) LLQ_TRACE_AT(4, it);
+          if (!mbar_wait(&a_full[tile * AS + sa], (it / AS) & 1, abort_flag, 0x230 + sa)) { ok = false; break; }
+          if (tile == 0) LLQ_TRACE_AT(5, it);
           tc_fence_after();
-          const uint32_t bbase = smem_u32(sb + s * C::B_STAGE_BYTES);
-          const uint32_t a_stage = a_base + sa * C::A_STAGE_COLS;
+          // descriptors advance by plain adds on the 16-byte-unit start address
+          const uint64_t bdesc0 = make_sdesc(smem_u32(sb + s * C::B_STAGE_BYTES));
+          const uint64_t half_step = static_cast<uint64_t>((box * 128) >> 4);
+          const uint32_t a_stage = a_base + sa * C::A_STAGE_COLS + tile * (KC / 2);
+          const uint32_t d = tile ? d1 : d0;
+          const uint32_t first = FAST ? 0u : (kc > 0 ? 1u : 0u);
 #pragma unroll
-          for (int j = 0; j < KC / 16; ++j) {
-            const uint64_t bdesc = make_sdesc(bbase + (j >> 2) * box * 128 + (j & 3) * 32);
-            const uint32_t acc = FAST ? (j > 0 ? 1u : 0u) : ((kc > 0 || j > 0) ? 1u : 0u);
-            tc_mma(d0, a_stage + j * 8, bdesc, idesc, acc);
-            tc_mma(d1, a_stage + KC / 2 + j * 8, bdesc, idesc, acc);
+          for (int jj = 0; jj < KC / 16 / SPLIT; ++jj) {
+            const int j = jj * SPLIT + par;
+            const uint64_t bdesc = bdesc0 + (j >> 2) * half_step + (j & 3) * 2;
+            const uint32_t acc = jj > 0 ? 1u : first;
+            if (!(args.debug & 2)) tc_mma(d, a_stage + j * 8, bdesc, idesc, acc);
           }
-          tc_commit(&a_empty[sa]);
-          tc_commit(&empty[s]);
-          if (FAST) tc_commit(&acc_full[it & 1]);
-          else if (kc == kch - 1) tc_commit(&acc_full[0]);
+          tc_commit(&mdone[s]);
+          if (tile == 0) LLQ_TRACE_AT(6, it);
+          if (!FAST && kc == kch - 1) tc_commit(&acc_full[0]);
         }
       }
     }
   } else if (warp < FIRST_EPI) {
     // ------------------------------------------------------------- dequant
-    const int wg = (warp - FIRST_DQ) >> 2;  // 0: tile 0, 1: tile 1
+    const int wgi = (warp - FIRST_DQ) >> 2;
+    const int wg = wgi & 1;                 // weight tile
+    const int part = wgi >> 1;              // which share of the row's chunks
+    const int c_lo = part * (C::CHUNKS / C::DQ_PARTS), c_hi = c_lo + C::CHUNKS / C::DQ_PARTS;
     const int q = warp & 3;                 // TMEM lane quarter
     const int r = q * 32 + lane;            // row within the tile
     const uint32_t a_row = tmem + C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16) + wg * (KC / 2);
@@ -521,38 +588,56 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int kc = 0; kc < kch; ++kc, ++it) {
         const int s = it % S, sa = it % AS;
         if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, 0x310 + s)) { ok = false; break; }
-        if (!mbar_wait(&a_empty[sa], ((it / AS) & 1) ^ 1, abort_flag, 0x320 + sa)) { ok = false; break; }
-        tc_fence_after();
+        if (warp == FIRST_DQ) LLQ_TRACE_AT(1, it);
         const uint8_t* wt = sw + s * C::W_STAGE_BYTES + wg * C::W_TILE_BYTES + r * C::W_ROW_BYTES;
         const uint32_t a_stage = a_row + sa * C::A_STAGE_COLS;
-        if (BITS == 4) {
-          const float sc = FAST ? 0.f : srow[args.group > 0 ? (kc * KC) / args.group : 0];
+        // this row's packed bytes into registers, then hand the weight slot back
+        // to the producer at once; only the token tile waits for the MMA
+        constexpr int MYC = C::CHUNKS / C::DQ_PARTS;
+        uint4 v[MYC];
 #pragma unroll
-          for (int c = 0; c < C::CHUNKS; ++c) {
-            const uint4 v = *reinterpret_cast<const uint4*>(wt + ((c ^ ((r >> 1) & 3)) * 16));
+        for (int ci = 0; ci < MYC; ++ci) {
+          const int c = c_lo + ci;
+          const int pc = BITS == 4 ? (c ^ ((r >> 1) & 3)) : (c ^ (r & 7));  // 64/128-byte swizzle
+          v[ci] = *reinterpret_cast<const uint4*>(wt + pc * 16);
+        }
+        const float sc = FAST ? 0.f : srow[args.group > 0 ? (kc * KC) / args.group : 0];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&wfree[s]);
+        // the TMEM A stage is free once the MMAs of step it - AS completed
+        if (it >= AS) {
+          const int pit = it - AS;
+          if (!mbar_wait(&mdone[pit % S], (pit / S) & 1, abort_flag, 0x320 + sa)) { ok = false; break; }
+        }
+        if (warp == FIRST_DQ) LLQ_TRACE_AT(2, it);
+        tc_fence_after();
+        if (BITS == 4) {
+#pragma unroll
+          for (int ci = 0; ci < MYC; ++ci) {
             uint32_t o[16];
-            if (FAST) codes_int4(v, o);
-            else dequant_int4_exact(v, sc, o);
-            tc_st16(a_stage + c * 16, o);
+            if (args.debug & 1) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) o[i] = (i & 1) ? v[ci].y : v[ci].x;
+            } else if (FAST) codes_int4(v[ci], o);
+            else dequant_int4_exact(v[ci], sc, o);
+            if (!(args.debug & 4)) tc_st16(a_stage + (c_lo + ci) * 16, o);
+            else asm volatile("" ::"r"(o[0]), "r"(o[5]), "r"(o[10]), "r"(o[15]));
           }
         } else {
-          const float sc = srow[args.group > 0 ? (kc * KC) / args.group : 0];
 #pragma unroll
-          for (int c = 0; c < C::CHUNKS; c += 2) {
-            const uint4 v0 = *reinterpret_cast<const uint4*>(wt + ((c ^ (r & 7)) * 16));
-            const uint4 v1 = *reinterpret_cast<const uint4*>(wt + (((c + 1) ^ (r & 7)) * 16));
+          for (int ci = 0; ci < MYC; ci += 2) {
             uint32_t o[16];
-            dequant_int8_exact(v0, sc, o);
-            dequant_int8_exact(v1, sc, o + 8);
-            tc_st16(a_stage + c * 8, o);
+            dequant_int8_exact(v[ci], sc, o);
+            dequant_int8_exact(v[ci + 1], sc, o + 8);
+            tc_st16(a_stage + (c_lo + ci) * 8, o);
           }
         }
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&a_full[sa]);
-          mbar_arrive(&empty[s]);
+          mbar_arrive(&a_full[wg * AS + sa]);
+          if (warp == FIRST_DQ) LLQ_TRACE_AT(3, it);
         }
       }
       __syncwarp();
@@ -595,12 +680,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         float acc0[FAST ? HALF : 1], acc1[FAST ? HALF : 1];
 #pragma unroll
         for (int i = 0; i < (FAST ? HALF : 1); ++i) acc0[i] = acc1[i] = 0.f;
-        if (!mbar_wait(&sc_full[sbuf], (ii >> 1) & 1, abort_flag, 0x400)) break;
+        if (!mbar_wait_sleep(&sc_full[sbuf], (ii >> 1) & 1, abort_flag, 0x400)) break;
         const float* s0row = ssc + sbuf * (2 * ROWS * MAX_G) + r * G;
         const float* s1row = s0row + ROWS * MAX_G;
         for (int kc = 0; kc < kch; ++kc, ++it) {
           const int pb = it & 1;
-          if (!mbar_wait(&acc_full[pb], (it >> 1) & 1, abort_flag, 0x410 + pb)) { ok = false; break; }
+          if (!mbar_wait(&mdone[it % S], (it / S) & 1, abort_flag, 0x410 + pb)) { ok = false; break; }
           tc_fence_after();
           const int gi = args.group > 0 ? (kc * KC) / args.group : 0;
           const float s0 = s0row[gi], s1 = s1row[gi];
@@ -629,7 +714,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int i = 0; i < (FAST ? HALF : 1); ++i) emit(t_begin + i, acc0[i], acc1[i]);
       } else {
-        if (!mbar_wait(&acc_full[0], ii & 1, abort_flag, 0x420)) break;
+        if (!mbar_wait_sleep(&acc_full[0], ii & 1, abort_flag, 0x420)) break;
         tc_fence_after();
 #pragma unroll
         for (int c = 0; c < HALF / 8; ++c) {
@@ -637,7 +722,17 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (t0 < t_end) {
             float v0[8], v1[8];
             tc_ld8(tmem + lane_addr + t0, v0);
-            tc_ld8(tmem + lane_addr + NTM + t0, v1);
+            tc_ld8(tmem + lane_addr + SPLIT * NTM + t0, v1);
+            if (SPLIT == 2) {
+              float w0[8], w1[8];
+              tc_ld8(tmem + lane_addr + NTM + t0, w0);
+              tc_ld8(tmem + lane_addr + 3 * NTM + t0, w1);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                v0[i] = __fadd_rn(v0[i], w0[i]);
+                v1[i] = __fadd_rn(v1[i], w1[i]);
+              }
+            }
 #pragma unroll
             for (int i = 0; i < 8; ++i) emit(t0 + i, v0[i], v1[i]);
           }
@@ -721,6 +816,11 @@ int launch_tc(const void* act, int64_t n_rows, const int32_t* offsets, int E, in
   const bool grouped = group_size > 0 && K % group_size == 0;
   a.group = grouped ? group_size : 0;
   a.groups = grouped ? K / group_size : 1;
+  static const int debug_flags = [] {
+    const char* e = getenv("LLQ_TC_DEBUG");
+    return e ? atoi(e) : 0;
+  }();
+  a.debug = debug_flags;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(moe_gemm_tc_kernel<GEMM1, BITS, FAST, NTM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -728,7 +828,7 @@ int launch_tc(const void* act, int64_t n_rows, const int32_t* offsets, int E, in
     attr = true;
   }
   const int grid = num_sms();
-  moe_gemm_tc_kernel<GEMM1, BITS, FAST, NTM><<<grid, THREADS, C::SMEM_BYTES, st>>>(tw, tb[0], tb[1], tb[2],
+  moe_gemm_tc_kernel<GEMM1, BITS, FAST, NTM><<<grid, C::THREADS, C::SMEM_BYTES, st>>>(tw, tb[0], tb[1], tb[2],
                                                                                   tb[3], a);
   return check_launch("moe_gemm_tc_kernel");
 }
@@ -792,3 +892,9 @@ int gemm2_tc(const void* h_sorted, const int32_t* offsets, const int32_t* sorted
 }
 
 }  // namespace llq
+
+#ifdef LLQ_TRACE
+extern "C" int llq_trace_read(long long* host) {
+  return cudaMemcpyFromSymbol(host, llq::g_tc_trace, sizeof(long long) * 8 * 64) == cudaSuccess ? 0 : 3;
+}
+#endif

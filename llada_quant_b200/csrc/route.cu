@@ -83,7 +83,7 @@ __device__ void warp_softmax_topk(float (&v)[kMaxExperts / 32], int E, int k, in
 }
 
 // logits + softmax + top-k for kRouteTokens tokens per block.
-__global__ void __launch_bounds__(256) route_kernel(const __nv_bfloat16* __restrict__ x,
+__global__ void __launch_bounds__(512) route_kernel(const __nv_bfloat16* __restrict__ x,
                                                     const __nv_bfloat16* __restrict__ gate_w,
                                                     int64_t T, int H, int E, int k,
                                                     const float* __restrict__ bias, int renormalize,
@@ -107,27 +107,53 @@ __global__ void __launch_bounds__(256) route_kernel(const __nv_bfloat16* __restr
   }
   __syncthreads();
 
-  for (int e = warp; e < E; e += blockDim.x / 32) {
-    float acc[kRouteTokens];
+  // Each warp owns experts warp, warp + nwarps, ...; two experts at a time,
+  // with every 16-byte weight load of a lane issued before any is consumed, so
+  // that a warp waits for L2 about once per pair instead of once per vector.
+  const int nwarps = blockDim.x >> 5;
+  constexpr int U = 8;  // vectors per lane per pass (H = 2048 -> one pass)
+  for (int e0 = warp; e0 < E; e0 += 2 * nwarps) {
+    const int e1 = e0 + nwarps;
+    float acc0[kRouteTokens], acc1[kRouteTokens];
 #pragma unroll
-    for (int t = 0; t < kRouteTokens; ++t) acc[t] = 0.f;
-    const uint4* wrow = reinterpret_cast<const uint4*>(gate_w + static_cast<int64_t>(e) * H);
-    for (int v = lane; v < vec_per_row; v += 32) {
-      const uint4 wv = __ldg(wrow + v);
-      const __nv_bfloat16* wp = reinterpret_cast<const __nv_bfloat16*>(&wv);
+    for (int t = 0; t < kRouteTokens; ++t) acc0[t] = acc1[t] = 0.f;
+    const uint4* w0 = reinterpret_cast<const uint4*>(gate_w + static_cast<int64_t>(e0) * H);
+    const uint4* w1 = reinterpret_cast<const uint4*>(gate_w + static_cast<int64_t>(e1 < E ? e1 : e0) * H);
+    for (int vb = 0; vb < vec_per_row; vb += 32 * U) {
+      uint4 a[U], b[U];
 #pragma unroll
-      for (int t = 0; t < kRouteTokens; ++t) {
-        const uint4 xv = reinterpret_cast<const uint4*>(xs + static_cast<int64_t>(t) * H)[v];
-        const __nv_bfloat16* xp = reinterpret_cast<const __nv_bfloat16*>(&xv);
+      for (int u = 0; u < U; ++u) {
+        const int v = vb + lane + 32 * u;
+        a[u] = v < vec_per_row ? __ldg(w0 + v) : make_uint4(0, 0, 0, 0);
+        b[u] = (v < vec_per_row && e1 < E) ? __ldg(w1 + v) : make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          acc[t] = __fmaf_rn(__bfloat162float(xp[i]), __bfloat162float(wp[i]), acc[t]);
+      for (int u = 0; u < U; ++u) {
+        const int v = vb + lane + 32 * u;
+        if (v >= vec_per_row) break;
+        const __nv_bfloat16* ap = reinterpret_cast<const __nv_bfloat16*>(&a[u]);
+        const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(&b[u]);
+#pragma unroll
+        for (int t = 0; t < kRouteTokens; ++t) {
+          const uint4 xv = reinterpret_cast<const uint4*>(xs + static_cast<int64_t>(t) * H)[v];
+          const __nv_bfloat16* xp = reinterpret_cast<const __nv_bfloat16*>(&xv);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float xf = __bfloat162float(xp[i]);
+            acc0[t] = __fmaf_rn(xf, __bfloat162float(ap[i]), acc0[t]);
+            acc1[t] = __fmaf_rn(xf, __bfloat162float(bp[i]), acc1[t]);
+          }
+        }
       }
     }
 #pragma unroll
     for (int t = 0; t < kRouteTokens; ++t) {
-      const float l = round_bf16(warp_sum(acc[t]));
-      if (lane == 0) lg[t * E + e] = l;
+      const float l0 = round_bf16(warp_sum(acc0[t]));
+      const float l1 = round_bf16(warp_sum(acc1[t]));
+      if (lane == 0) {
+        lg[t * E + e0] = l0;
+        if (e1 < E) lg[t * E + e1] = l1;
+      }
     }
   }
   __syncthreads();
@@ -270,6 +296,86 @@ __global__ void __launch_bounds__(kAlignThreads) align_scatter_kernel(
 
 // kperm: reorder each 8-element block as [0,4,1,5,2,6,3,7], the K order in
 // which the fast-mode expert GEMM lays out its integer weight codes
+// Small problems (the decode regime): count, scan and stable scatter in one
+// block of 1024 threads, one launch instead of three.
+constexpr int kAlignSmallMax = 16384;
+constexpr int kAlignSmallThreads = 1024;
+
+__global__ void __launch_bounds__(kAlignSmallThreads) align_small_kernel(
+    const int32_t* __restrict__ ids, int n, int E, int32_t* __restrict__ offsets,
+    int32_t* __restrict__ sorted_slots) {
+  constexpr int W = kAlignSmallThreads / 32;
+  __shared__ int32_t cnt[kMaxExperts];
+  __shared__ int32_t cursor[kMaxExperts];
+  __shared__ int32_t wcnt[W][kMaxExperts];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < kMaxExperts; i += blockDim.x) cnt[i] = 0;
+  for (int i = tid; i < W * kMaxExperts; i += blockDim.x) (&wcnt[0][0])[i] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += blockDim.x) {
+    const int e = ids[i];
+    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+    else atomicExch(&g_device_error, 2);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    constexpr int J = kMaxExperts / 32;
+    int local[J], sum = 0;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int e = lane * J + j;
+      local[j] = e < E ? cnt[e] : 0;
+      sum += local[j];
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    int run = incl - sum;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int e = lane * J + j;
+      if (e < E) {
+        cursor[e] = run;
+        offsets[e] = run;
+      }
+      run += local[j];
+    }
+    if (lane == 31) offsets[E] = incl;
+  }
+  __syncthreads();
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int r0 = 0; r0 < n; r0 += blockDim.x) {
+    const int i = r0 + tid;
+    int e = -1;
+    if (i < n) {
+      e = ids[i];
+      if (e < 0 || e >= E) e = -1;
+    }
+    const unsigned same = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(same & lt_mask);
+    if (e >= 0 && rank == 0) wcnt[warp][e] = __popc(same);
+    __syncthreads();
+    if (e >= 0) {
+      int pos = cursor[e] + rank;
+      for (int w = 0; w < warp; ++w) pos += wcnt[w][e];
+      sorted_slots[pos] = i;
+    }
+    __syncthreads();
+    for (int ee = tid; ee < E; ee += blockDim.x) {
+      int add = 0;
+      for (int w = 0; w < W; ++w) {
+        add += wcnt[w][ee];
+        wcnt[w][ee] = 0;
+      }
+      cursor[ee] += add;
+    }
+    __syncthreads();
+  }
+}
+
 template <bool KPERM>
 __global__ void permute_kernel(const uint4* __restrict__ x, int64_t n_rows, int vec_per_row, int k,
                                const int32_t* __restrict__ sorted_slots, uint4* __restrict__ xs) {
@@ -339,7 +445,7 @@ int route_impl(const void* x, const void* gate_w, int64_t T, int H, int E, int k
     attr_set = true;
   }
   const unsigned blocks = static_cast<unsigned>((T + kRouteTokens - 1) / kRouteTokens);
-  route_kernel<<<blocks, 256, smem, st>>>(static_cast<const __nv_bfloat16*>(x),
+  route_kernel<<<blocks, 512, smem, st>>>(static_cast<const __nv_bfloat16*>(x),
                                           static_cast<const __nv_bfloat16*>(gate_w), T, H, E, k,
                                           bias, renormalize, static_cast<__nv_bfloat16*>(logits),
                                           topk_w, topk_ids);
@@ -377,6 +483,10 @@ int align_impl(const int32_t* ids, int64_t T, int k, int E, int32_t* offsets, in
   if (n == 0) {
     cudaMemsetAsync(offsets, 0, sizeof(int32_t) * (E + 1), st);
     return check_launch("align memset");
+  }
+  if (n <= kAlignSmallMax) {
+    align_small_kernel<<<1, kAlignSmallThreads, 0, st>>>(ids, static_cast<int>(n), E, offsets, sorted_slots);
+    return check_launch("align_small_kernel");
   }
   const int64_t nblk = (n + kAlignChunk - 1) / kAlignChunk;
   if (nblk > 0x7fffffff) return fail(LLQ_EINVAL, "too many entries");

@@ -1,0 +1,93 @@
+"""Expert parallelism: the routed MoE layer with experts sharded across ranks.
+
+Rank ``r`` of ``R`` owns the contiguous experts ``[r*E/R, (r+1)*E/R)`` (their
+packed ``_qw*``/``_sw*`` slices); the router is replicated and tokens are
+data-parallel.  One layer call on each rank:
+
+1. route its own tokens (global expert ids, fp32 routed weights);
+2. group its ``T*k`` (token, slot) entries by destination rank (stable);
+3. exchange per-destination counts, then the token rows and their
+   (local expert id, routed weight) -- NCCL ``all_to_all_single`` over
+   NVLink/NVSwitch, one flat stage;
+4. run the local experts on the received rows as a top-1 layer (the routed
+   weight is applied inside GEMM2, exactly as on one GPU);
+5. send the per-(token, slot) results back with the inverse all-to-all and
+   combine each token's ``k`` slots in slot order.
+
+Because every (token, slot) result is computed by the same kernels on the
+same row, and the slots are summed in the same order, the output equals the
+single-GPU layer bit for bit.  The collective plumbing is plain
+``torch.distributed`` (backend nccl on GPUs, gloo in the CPU tests, where a
+caller-supplied ``local_fn`` stands in for the kernels).
+"""
+
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+LocalFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
+
+
+def _exchange(t: torch.Tensor, out_splits, in_splits, group) -> torch.Tensor:
+    out = t.new_empty((sum(out_splits),) + tuple(t.shape[1:]))
+    dist.all_to_all_single(out, t.contiguous(), output_split_sizes=list(out_splits),
+                           input_split_sizes=list(in_splits), group=group)
+    return out
+
+
+def ep_dispatch_combine(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor,
+                        experts_per_rank: int, local_fn: LocalFn, group=None) -> torch.Tensor:
+    """Steps 2-5 above.  ``local_fn(rows, local_expert_ids, routed_w) -> rows`` computes
+    ``routed_w * expert(row)`` (bf16) for each received row."""
+    world = dist.get_world_size(group)
+    T, H = x.shape
+    k = topk_ids.shape[1]
+    ids = topk_ids.reshape(-1).to(torch.int64)
+    dest = torch.div(ids, experts_per_rank, rounding_mode="floor")
+    order = torch.argsort(dest, stable=True)                     # sorted (token, slot) entries
+    send_counts = torch.bincount(dest, minlength=world)
+    recv_counts = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv_counts, send_counts, group=group)
+    sc = send_counts.tolist()
+    rc = recv_counts.tolist()
+    rows = x.index_select(0, torch.div(order, k, rounding_mode="floor"))
+    meta = torch.stack([(ids[order] - dest[order] * experts_per_rank).to(torch.int32),
+                        topk_w.reshape(-1)[order].to(torch.float32).view(torch.int32)], dim=1)
+    recv_rows = _exchange(rows, rc, sc, group)
+    recv_meta = _exchange(meta, rc, sc, group)
+    if recv_rows.shape[0]:
+        y = local_fn(recv_rows, recv_meta[:, 0].contiguous(), recv_meta[:, 1].contiguous().view(torch.float32))
+    else:
+        y = recv_rows.new_empty((0, H))
+    back = _exchange(y.to(x.dtype), sc, rc, group)
+    y_slots = x.new_zeros((T * k, H))
+    y_slots.index_copy_(0, order, back)
+    # combine in slot order, fp32 sum, one rounding (as the single-GPU combine)
+    acc = torch.zeros((T, H), dtype=torch.float32, device=x.device)
+    ys = y_slots.view(T, k, H)
+    for j in range(k):
+        acc += ys[:, j].float()
+    return acc.to(x.dtype)
+
+
+def local_packed_fn(packed, impl: int) -> LocalFn:
+    """The local experts through the B200 kernels, as a top-1 layer."""
+    from . import ops
+
+    def fn(rows: torch.Tensor, local_ids: torch.Tensor, routed_w: torch.Tensor) -> torch.Tensor:
+        return ops.fused_moe_packed(rows, packed.qw1, packed.sw1, packed.qw2, packed.sw2,
+                                    routed_w.view(-1, 1), local_ids.view(-1, 1), packed.bits, impl)
+    return fn
+
+
+def ep_moe_layer(x: torch.Tensor, gate_w: torch.Tensor, packed, top_k: int, rank: int, world: int,
+                 bias: Optional[torch.Tensor] = None, renormalize: bool = False, impl: int = 0,
+                 group=None) -> torch.Tensor:
+    """One expert-parallel MoE layer on this rank's tokens ``x`` [T_r, H]."""
+    from . import ops
+    topk_w, topk_ids, _ = ops.route(x, gate_w, top_k, bias, renormalize)
+    return ep_dispatch_combine(x, topk_w, topk_ids, packed.num_experts, local_packed_fn(packed, impl),
+                               group=group)

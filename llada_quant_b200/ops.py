@@ -225,18 +225,19 @@ def _(topk_ids, num_experts):
 
 
 @torch.library.custom_op("llada_quant::moe_permute", mutates_args=())
-def moe_permute(x: torch.Tensor, sorted_slots: torch.Tensor, k: int) -> torch.Tensor:
+def moe_permute(x: torch.Tensor, sorted_slots: torch.Tensor, k: int, kperm: bool = False) -> torch.Tensor:
+    """Rows of ``x`` in expert order; ``kperm`` also applies the fast-mode K order."""
     _need_cuda(x, sorted_slots)
     x = x.contiguous()
     T, H = x.shape
     out = torch.empty(sorted_slots.numel(), H, dtype=x.dtype, device=x.device)
-    check(load().llq_moe_permute(x.data_ptr(), T, H, k, sorted_slots.data_ptr(), out.data_ptr(),
-                                 _stream(x)), "moe_permute")
+    check(load().llq_moe_permute(x.data_ptr(), T, H, k, sorted_slots.data_ptr(), int(kperm),
+                                 out.data_ptr(), _stream(x)), "moe_permute")
     return out
 
 
 @moe_permute.register_fake
-def _(x, sorted_slots, k):
+def _(x, sorted_slots, k, kperm=False):
     return x.new_empty(sorted_slots.shape[0], x.shape[1])
 
 

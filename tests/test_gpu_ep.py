@@ -1,0 +1,79 @@
+"""Expert parallelism on real GPUs (NCCL), when the box has at least two.
+
+Each rank holds a contiguous expert shard and its own tokens; the assembled
+output must match the single-GPU layer on all tokens (same kernels, same
+per-row arithmetic, same slot order) -- bit for bit is expected, the bar is
+the layer tolerance of the other MoE tests.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+E, H, I, K, T_RANK = 64, 2048, 1024, 8, 128
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, path):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    from llada_quant_b200 import symmetric as G
+    from llada_quant_b200.ep import ep_moe_layer
+    from llada_quant_b200.moe import PackedExperts
+    g = torch.Generator().manual_seed(0)
+    w1 = (torch.randn(E, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(E, H, I, generator=g) * 0.02).to(torch.bfloat16)
+    gate_w = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    x = torch.randn(world * T_RANK, H, generator=g).to(torch.bfloat16).cuda()
+    epr = E // world
+    sl = slice(rank * epr, (rank + 1) * epr)
+    r1 = G.quantize_tensor(w1[sl].contiguous().cuda(), bits=4, group_size=128)
+    r2 = G.quantize_tensor(w2[sl].contiguous().cuda(), bits=4, group_size=128)
+    packed = PackedExperts(r1.q, r1.scale, r2.q, r2.scale, 4, 128)
+    out = ep_moe_layer(x[rank * T_RANK:(rank + 1) * T_RANK].contiguous(), gate_w, packed, K, rank, world)
+    torch.cuda.synchronize()
+    np.save(f"{path}.{rank}.npy", out.float().cpu().numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_ep_matches_single_gpu(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    from llada_quant_b200 import symmetric as G
+    from llada_quant_b200.fused_moe import moe_layer
+    from llada_quant_b200.moe import PackedExperts
+    from oracle import moe as M
+    world = 2
+    path = str(tmp_path / "ep")
+    mp.start_processes(_worker, args=(world, _port(), path), nprocs=world, join=True, start_method="spawn")
+    got = np.concatenate([np.load(f"{path}.{r}.npy") for r in range(world)])
+    g = torch.Generator().manual_seed(0)
+    w1 = (torch.randn(E, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(E, H, I, generator=g) * 0.02).to(torch.bfloat16)
+    gate_w = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    x = torch.randn(world * T_RANK, H, generator=g).to(torch.bfloat16).cuda()
+    r1 = G.quantize_tensor(w1.cuda(), bits=4, group_size=128)
+    r2 = G.quantize_tensor(w2.cuda(), bits=4, group_size=128)
+    ref = moe_layer(x, gate_w, PackedExperts(r1.q, r1.scale, r2.q, r2.scale, 4, 128), K).float().cpu().numpy()
+    assert M.rel_l2(got, ref) <= 3e-3
+    assert M.max_abs(got, ref) <= 2 * 2.0 ** -7 * np.abs(ref).max()
+    print("bitwise equal:", np.array_equal(got, ref))

@@ -98,3 +98,16 @@ def test_permute_and_combine_exact():
     for j in range(k):
         ref = (ref + yn[:, j]).astype(np.float32)
     assert np.array_equal(to_np(out), S.round_to_bf16(ref))
+
+
+def test_permute_kperm_reorders_each_8_block():
+    from llada_quant_b200 import ops
+    T, H, E, k = 9, 64, 4, 2
+    _, ids = random_routing(T, E, k, seed=2)
+    x = torch.randn(T, H).to(torch.bfloat16)
+    offsets, slots = ops.moe_align(torch.from_numpy(ids).cuda(), E)
+    plain = ops.moe_permute(x.cuda(), slots, k).cpu()
+    perm = ops.moe_permute(x.cuda(), slots, k, True).cpu()
+    order = torch.tensor([0, 4, 1, 5, 2, 6, 3, 7])
+    idx = (torch.arange(H) // 8) * 8 + order.repeat(H // 8)
+    assert torch.equal(perm, plain[:, idx])
