@@ -342,7 +342,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             v, cores, dt = cpu_reference(1)
             cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
                    "sample": f"one C3 layer call (256 tokens) of the numpy port of the reference CPU path, {dt:.1f} s"}
-        launches_per_step = 8 if world == 1 else None
+        # ours per step: router, align, permute, GEMM1, GEMM2, combine (+ the expert-parallel
+        # grouping, gather and slot combine at N > 1)
+        launches_per_step = 6 if world == 1 else 9
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,

@@ -47,13 +47,21 @@ def ep_dispatch_combine(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.T
     k = topk_ids.shape[1]
     ids = topk_ids.reshape(-1).to(torch.int64)
     dest = torch.div(ids, experts_per_rank, rounding_mode="floor")
-    order = torch.argsort(dest, stable=True)                     # sorted (token, slot) entries
-    send_counts = torch.bincount(dest, minlength=world)
+    if x.is_cuda:
+        # the package's own stable grouping, row gather and slot combine
+        from . import ops
+        offsets, order32 = ops.moe_align(dest.view(T, k).to(torch.int32), world)
+        send_counts = (offsets[1:] - offsets[:-1]).to(torch.int64)
+        order = order32.to(torch.int64)
+        rows = ops.moe_permute(x, order32, k)
+    else:
+        order = torch.argsort(dest, stable=True)                 # sorted (token, slot) entries
+        send_counts = torch.bincount(dest, minlength=world)
+        rows = x.index_select(0, torch.div(order, k, rounding_mode="floor"))
     recv_counts = torch.empty_like(send_counts)
     dist.all_to_all_single(recv_counts, send_counts, group=group)
-    sc = send_counts.tolist()
-    rc = recv_counts.tolist()
-    rows = x.index_select(0, torch.div(order, k, rounding_mode="floor"))
+    counts = torch.stack([send_counts, recv_counts]).tolist()    # the one host sync: NCCL split sizes
+    sc, rc = counts[0], counts[1]
     meta = torch.stack([(ids[order] - dest[order] * experts_per_rank).to(torch.int32),
                         topk_w.reshape(-1)[order].to(torch.float32).view(torch.int32)], dim=1)
     recv_rows = _exchange(rows, rc, sc, group)
@@ -63,8 +71,11 @@ def ep_dispatch_combine(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.T
     else:
         y = recv_rows.new_empty((0, H))
     back = _exchange(y.to(x.dtype), sc, rc, group)
-    y_slots = x.new_zeros((T * k, H))
+    y_slots = x.new_empty((T * k, H))
     y_slots.index_copy_(0, order, back)
+    if x.is_cuda:
+        from . import ops
+        return ops.moe_combine(y_slots, k)
     # combine in slot order, fp32 sum, one rounding (as the single-GPU combine)
     acc = torch.zeros((T, H), dtype=torch.float32, device=x.device)
     ys = y_slots.view(T, k, H)
