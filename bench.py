@@ -364,6 +364,73 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         print(json.dumps(line), flush=True)
 
 
+C4_TOKENS, C4_LAYERS = 32 * 1024, 16
+
+
+def c4_flops() -> float:
+    """Algorithmic FLOPs of one C4 step: 16 layers x (router + GEMM1 + GEMM2) over 32768 tokens."""
+    per_layer = 2.0 * C4_TOKENS * TOPK * (2 * I * H + H * I) + 2.0 * C4_TOKENS * H * E
+    return per_layer * C4_LAYERS
+
+
+def run_c4(args):
+    """16 chained C3-shaped layers (x <- x + moe_l(x)) over 32768 tokens on one
+    GPU; attention/norms are outside the hot path and not modelled.  Metric: tokens/s of the stack,
+    with TFLOP/s against the measured dense bf16 peak."""
+    import torch
+    from llada_quant_b200 import ops
+    from llada_quant_b200.fused_moe import IMPL
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    layers, gate_w = make_layers(device, C4_LAYERS, E, 0)
+    x0 = torch.randn(C4_TOKENS, H, generator=torch.Generator(device=device).manual_seed(2),
+                     device=device).to(torch.bfloat16)
+    impl = IMPL[args.gemm]
+
+    def step():
+        x = x0
+        for lay in layers:
+            tw, ids, _ = ops.route(x, gate_w, TOPK, None, False)
+            y = ops.fused_moe_packed(x, lay.qw1, lay.sw1, lay.qw2, lay.sw2, tw, ids, BITS, impl)
+            x = x + y
+        return x
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        s0.record()
+        for _ in range(args.steps):
+            step()
+        s1.record()
+        torch.cuda.synchronize()
+    ms = s0.elapsed_time(s1) / args.steps
+    tflops = c4_flops() / (ms / 1e3) / 1e12
+    peak = None
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops_sustained"])
+        kind = "measured (sustained)"
+    except Exception:
+        peak, kind = 1400.0, "fallback (sustained)"
+    line = {
+        "metric": "W4A16 MoE stack tokens/s (LLaDA-MoE-7B-A1B, 16 layers, batch 32 x seq 1024)",
+        "value": C4_TOKENS / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int4 weights, bf16 activations, fp32 accumulate",
+        "data": "synthetic (seeded N(0,0.02) weights quantized on device, N(0,1) tokens)",
+        "config": {"workload": "C4 16-layer MoE stack, T=32768, E=64 H=2048 I=1024 top-8 W4A16 g128",
+                   "gemm": args.gemm, "l2": "inputs larger than L2 (16 layer weight sets, 3.4 GB)"},
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(tflops / peak, 4), "peak_source": kind, "traffic": None,
+                     "algorithmic_flops": c4_flops()},
+        "gpu_launches": 7 * C4_LAYERS * args.steps,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def kernel_case(args):
     """One C3 layer weight set, route -> align -> permute -> GEMM1 -> GEMM2 -> combine, twice."""
     import torch
@@ -394,6 +461,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--gemm", choices=["auto", "tcgen05", "tcgen05_fast", "simt"], default="auto")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--workload", choices=["c3", "c4"], default="c3",
+                    help="c3: one LLaDA-MoE layer at 256 tokens (default, HBM-bound); c4: the 16-layer "
+                         "stack over batch 32 x seq 1024 tokens (tensor-bound)")
     ap.add_argument("--kernel-case", action="store_true",
                     help="run the C3 layer's kernels twice on one small input set and exit "
                          "(the command the ncu captures under profiles/ were taken on)")
@@ -406,6 +476,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.workload == "c4":
+        run_c4(args)
         return
     if world > 1:
         import torch

@@ -97,6 +97,8 @@ def _run_layer(T, E, H, I, k, bits, impl, skew=None, search="amax", seed=0):
     (33, 64, 2048, 1024, 8, 4),     # ragged, many empty experts
     (1, 16, 1024, 512, 2, 4),       # single token
     (7, 16, 1024, 512, 2, 8),
+    (2048, 16, 1024, 512, 2, 4),    # > 96 rows per expert: the 128-token prefill tiles
+    (2048, 16, 1024, 512, 2, 8),
 ])
 def test_fused_layer_matches_oracle(impl, T, E, H, I, k, bits):
     out, ref, truth = _run_layer(T, E, H, I, k, bits, impl)
