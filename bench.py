@@ -329,7 +329,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         achieved = algo / (k_ms / 1e3) / 1e9
         kernel = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                   "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                  "traffic": read_traffic(f"gemm1_{args.gemm}_c3.txt"), "kernel": "moe GEMM1 (W4A16, SiLU epilogue)",
+                  "traffic": read_traffic("gemm1_fast_c3.txt" if args.gemm == "tcgen05_fast" else "gemm1_exact_c3.txt"), "kernel": "moe GEMM1 (W4A16, SiLU epilogue)",
                   "algorithmic_bytes": algo, "launch_ms": round(k_ms, 5)}
         layer_algo = layer_bytes(T_PER_RANK, TOPK, int(round(hit)))
         layer_gbs = layer_algo / (ms_per_step / 1e3) / 1e9
