@@ -238,8 +238,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         x = xs[i % N_LAYERS]
         if world > 1:
             return ep.ep_moe_layer(x, gate_w, layer, TOPK, rank, world, bias=bias, impl=impl)
-        tw, ids, _ = ops.route(x, gate_w, TOPK, bias, False)
-        return ops.fused_moe_packed(x, layer.qw1, layer.sw1, layer.qw2, layer.sw2, tw, ids, BITS, impl)
+        tw, ids, _ = ops._route_impl(x, gate_w, TOPK, bias, False)
+        return ops._fused_moe_packed_impl(x, layer.qw1, layer.sw1, layer.qw2, layer.sw2, tw, ids, BITS, impl)
 
     def barrier():
         if world > 1:
@@ -390,8 +390,8 @@ def run_c4(args):
     def step():
         x = x0
         for lay in layers:
-            tw, ids, _ = ops.route(x, gate_w, TOPK, None, False)
-            y = ops.fused_moe_packed(x, lay.qw1, lay.sw1, lay.qw2, lay.sw2, tw, ids, BITS, impl)
+            tw, ids, _ = ops._route_impl(x, gate_w, TOPK, None, False)
+            y = ops._fused_moe_packed_impl(x, lay.qw1, lay.sw1, lay.qw2, lay.sw2, tw, ids, BITS, impl)
             x = x + y
         return x
 

@@ -145,6 +145,21 @@ int llq_moe_permute(const void* x, int64_t T, int H, int k, const int32_t* sorte
 /* Unpermute/combine: out[t] = bf16(sum_j y_slots[t*k + j]) in fp32, slot order. */
 int llq_moe_combine(const void* y_slots, int64_t T, int k, int H, void* out, void* stream);
 
+/*
+ * Expert parallelism (new work; the reference has no distributed MoE path --
+ * its external serving code only mentions rank-local experts,
+ * README.md:496-498).  llq_ep_pack: given sorted_slots from llq_moe_align over
+ * destination ranks (topk_ids / experts_per_rank), write each (token, slot)
+ * entry's row in that order, its expert id local to the destination rank, its
+ * routed weight, and inv_pos[token*k + slot] = its position.  llq_ep_combine:
+ * out[t] = bf16(sum_j back_rows[inv_pos[t*k + j]]) in fp32, slot order.
+ */
+int llq_ep_pack(const void* x, const int32_t* topk_ids, const float* topk_w, int64_t T, int k,
+                int H, int experts_per_rank, const int32_t* sorted_slots, void* send_rows,
+                int32_t* local_ids, float* weights, int32_t* inv_pos, void* stream);
+int llq_ep_combine(const void* back_rows, const int32_t* inv_pos, int64_t T, int k, int H,
+                   void* out, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Grouped W4A16 / W8A16 expert GEMMs over the packed buffers.                */
 /* ------------------------------------------------------------------------ */

@@ -38,6 +38,8 @@ SIGNATURES = {
     "llq_moe_align": (I, [P, L, I, I, P, P, P, c_size_t, P]),
     "llq_moe_permute": (I, [P, L, I, I, P, I, P, P]),
     "llq_moe_combine": (I, [P, L, I, I, P, P]),
+    "llq_ep_pack": (I, [P, P, P, L, I, I, I, P, P, P, P, P, P]),
+    "llq_ep_combine": (I, [P, P, L, I, I, P, P]),
     "llq_moe_gemm1": (I, [P, P, L, I, I, I, P, P, I, I, P, I, P]),
     "llq_moe_gemm2": (I, [P, P, P, P, L, I, I, I, P, P, I, I, P, I, P]),
     "llq_moe_workspace_size": (c_size_t, [L, I, I, I, I]),

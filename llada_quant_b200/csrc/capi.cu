@@ -44,6 +44,9 @@ size_t align_workspace_size(int64_t, int, int);
 int align_impl(const int32_t*, int64_t, int, int, int32_t*, int32_t*, void*, size_t, cudaStream_t);
 int permute_impl(const void*, int64_t, int, int, const int32_t*, void*, cudaStream_t, int);
 int combine_impl(const void*, int64_t, int, int, void*, cudaStream_t);
+int ep_pack_impl(const void*, const int32_t*, const float*, int64_t, int, int, int, const int32_t*, void*, int32_t*,
+                 float*, int32_t*, cudaStream_t);
+int ep_combine_impl(const void*, const int32_t*, int64_t, int, int, void*, cudaStream_t);
 int gemm1_simt(const void*, const int32_t*, int, int, int, const int8_t*, const float*, int, int,
                void*, cudaStream_t);
 int gemm2_simt(const void*, const int32_t*, const int32_t*, const float*, int, int, int,
@@ -156,6 +159,18 @@ int llq_moe_align(const int32_t* topk_ids, int64_t T, int k, int E, int32_t* exp
 int llq_moe_permute(const void* x, int64_t T, int H, int k, const int32_t* sorted_slots, int kperm,
                     void* x_sorted, void* stream) {
   return permute_impl(x, T, H, k, sorted_slots, x_sorted, as_stream(stream), kperm);
+}
+
+int llq_ep_pack(const void* x, const int32_t* topk_ids, const float* topk_w, int64_t T, int k, int H,
+                int experts_per_rank, const int32_t* sorted_slots, void* send_rows, int32_t* local_ids,
+                float* weights, int32_t* inv_pos, void* stream) {
+  return ep_pack_impl(x, topk_ids, topk_w, T, k, H, experts_per_rank, sorted_slots, send_rows, local_ids, weights,
+                      inv_pos, as_stream(stream));
+}
+
+int llq_ep_combine(const void* back_rows, const int32_t* inv_pos, int64_t T, int k, int H, void* out,
+                   void* stream) {
+  return ep_combine_impl(back_rows, inv_pos, T, k, H, out, as_stream(stream));
 }
 
 int llq_moe_combine(const void* y_slots, int64_t T, int k, int H, void* out, void* stream) {

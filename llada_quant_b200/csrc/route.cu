@@ -421,6 +421,57 @@ __global__ void combine_kernel(const uint4* __restrict__ y, int64_t T, int k, in
   }
 }
 
+// Expert-parallel dispatch: the rows of the (token, slot) entries in
+// destination-rank order (sorted_slots from the alignment over ranks), each
+// with its expert id local to the destination and its routed weight, plus the
+// position at which each entry leaves (to put the returned rows back).
+__global__ void ep_pack_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ topk_ids,
+                               const float* __restrict__ topk_w, int64_t n, int vec_per_row, int k,
+                               int experts_per_rank, const int32_t* __restrict__ sorted_slots,
+                               uint4* __restrict__ rows, int32_t* __restrict__ local_ids,
+                               float* __restrict__ weights, int32_t* __restrict__ inv_pos) {
+  const int64_t total = n * vec_per_row;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t p = i / vec_per_row;
+    const int v = static_cast<int>(i - p * vec_per_row);
+    const int32_t slot = sorted_slots[p];
+    rows[i] = __ldg(x + static_cast<int64_t>(slot / k) * vec_per_row + v);
+    if (v == 0) {
+      const int32_t e = topk_ids[slot];
+      local_ids[p] = e % experts_per_rank;
+      weights[p] = topk_w[slot];
+      inv_pos[slot] = static_cast<int32_t>(p);
+    }
+  }
+}
+
+// Expert-parallel combine: out[t] = bf16(sum_j back[inv_pos[t*k + j]]) in fp32, slot order.
+__global__ void ep_combine_kernel(const uint4* __restrict__ back, const int32_t* __restrict__ inv_pos,
+                                  int64_t T, int k, int vec_per_row, uint4* __restrict__ out) {
+  const int64_t total = T * vec_per_row;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / vec_per_row;
+    const int v = static_cast<int>(i - t * vec_per_row);
+    float acc[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const int64_t p = inv_pos[t * k + j];
+      const uint4 yv = __ldg(back + p * vec_per_row + v);
+      const __nv_bfloat16* yp = reinterpret_cast<const __nv_bfloat16*>(&yv);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] = __fadd_rn(acc[q], __bfloat162float(yp[q]));
+    }
+    uint4 o;
+    __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) op[q] = __float2bfloat16_rn(acc[q]);
+    out[i] = o;
+  }
+}
+
 inline unsigned grid_for(int64_t work, int threads) {
   int64_t b = (work + threads - 1) / threads;
   const int64_t cap = static_cast<int64_t>(num_sms()) * 32;
@@ -514,6 +565,29 @@ int permute_impl(const void* x, int64_t T, int H, int k, const int32_t* sorted_s
     permute_kernel<false><<<grid_for(n * vpr, 256), 256, 0, st>>>(static_cast<const uint4*>(x), n, vpr, k,
                                                                   sorted_slots, static_cast<uint4*>(xs));
   return check_launch("permute_kernel");
+}
+
+int ep_pack_impl(const void* x, const int32_t* topk_ids, const float* topk_w, int64_t T, int k, int H,
+                 int experts_per_rank, const int32_t* sorted_slots, void* rows, int32_t* local_ids,
+                 float* weights, int32_t* inv_pos, cudaStream_t st) {
+  if (H % 8 != 0) return fail(LLQ_EUNSUPPORTED, "hidden size must be a multiple of 8");
+  if (experts_per_rank < 1) return fail(LLQ_EINVAL, "experts_per_rank must be >= 1");
+  const int64_t n = T * k;
+  if (n == 0) return LLQ_OK;
+  const int vpr = H / 8;
+  ep_pack_kernel<<<grid_for(n * vpr, 256), 256, 0, st>>>(static_cast<const uint4*>(x), topk_ids, topk_w, n, vpr,
+                                                         k, experts_per_rank, sorted_slots,
+                                                         static_cast<uint4*>(rows), local_ids, weights, inv_pos);
+  return check_launch("ep_pack_kernel");
+}
+
+int ep_combine_impl(const void* back, const int32_t* inv_pos, int64_t T, int k, int H, void* out, cudaStream_t st) {
+  if (H % 8 != 0) return fail(LLQ_EUNSUPPORTED, "hidden size must be a multiple of 8");
+  if (T == 0) return LLQ_OK;
+  const int vpr = H / 8;
+  ep_combine_kernel<<<grid_for(T * vpr, 256), 256, 0, st>>>(static_cast<const uint4*>(back), inv_pos, T, k, vpr,
+                                                            static_cast<uint4*>(out));
+  return check_launch("ep_combine_kernel");
 }
 
 int combine_impl(const void* y, int64_t T, int k, int H, void* out, cudaStream_t st) {

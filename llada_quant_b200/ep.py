@@ -45,22 +45,16 @@ def ep_dispatch_combine(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.T
     world = dist.get_world_size(group)
     T, H = x.shape
     k = topk_ids.shape[1]
+    if x.is_cuda:
+        return _ep_cuda(x, topk_w, topk_ids, experts_per_rank, local_fn, group, world)
     ids = topk_ids.reshape(-1).to(torch.int64)
     dest = torch.div(ids, experts_per_rank, rounding_mode="floor")
-    if x.is_cuda:
-        # the package's own stable grouping, row gather and slot combine
-        from . import ops
-        offsets, order32 = ops.moe_align(dest.view(T, k).to(torch.int32), world)
-        send_counts = (offsets[1:] - offsets[:-1]).to(torch.int64)
-        order = order32.to(torch.int64)
-        rows = ops.moe_permute(x, order32, k)
-    else:
-        order = torch.argsort(dest, stable=True)                 # sorted (token, slot) entries
-        send_counts = torch.bincount(dest, minlength=world)
-        rows = x.index_select(0, torch.div(order, k, rounding_mode="floor"))
+    order = torch.argsort(dest, stable=True)                     # sorted (token, slot) entries
+    send_counts = torch.bincount(dest, minlength=world)
+    rows = x.index_select(0, torch.div(order, k, rounding_mode="floor"))
     recv_counts = torch.empty_like(send_counts)
     dist.all_to_all_single(recv_counts, send_counts, group=group)
-    counts = torch.stack([send_counts, recv_counts]).tolist()    # the one host sync: NCCL split sizes
+    counts = torch.stack([send_counts, recv_counts]).tolist()
     sc, rc = counts[0], counts[1]
     meta = torch.stack([(ids[order] - dest[order] * experts_per_rank).to(torch.int32),
                         topk_w.reshape(-1)[order].to(torch.float32).view(torch.int32)], dim=1)
@@ -73,9 +67,6 @@ def ep_dispatch_combine(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.T
     back = _exchange(y.to(x.dtype), sc, rc, group)
     y_slots = x.new_empty((T * k, H))
     y_slots.index_copy_(0, order, back)
-    if x.is_cuda:
-        from . import ops
-        return ops.moe_combine(y_slots, k)
     # combine in slot order, fp32 sum, one rounding (as the single-GPU combine)
     acc = torch.zeros((T, H), dtype=torch.float32, device=x.device)
     ys = y_slots.view(T, k, H)
@@ -84,13 +75,41 @@ def ep_dispatch_combine(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.T
     return acc.to(x.dtype)
 
 
+def _ep_cuda(x, topk_w, topk_ids, experts_per_rank, local_fn, group, world):
+    """The same steps on the package's kernels (called below the dispatcher): grouping over
+    ranks (moe_align), one pack kernel for rows + metadata, two NCCL all-to-alls out and one
+    back, the local layer, one combine kernel.  The single host synchronisation reads the
+    split sizes NCCL needs."""
+    from . import ops
+    T, H = x.shape
+    k = topk_ids.shape[1]
+    ids32 = topk_ids.to(torch.int32)
+    dest = torch.div(ids32, experts_per_rank, rounding_mode="floor")
+    offsets, order = ops._moe_align_impl(dest, world)
+    rows, lid, wts, inv = ops._ep_pack_impl(x, ids32, topk_w, order, experts_per_rank)
+    meta = torch.stack([lid, wts.view(torch.int32)], dim=1)
+    send_counts = (offsets[1:] - offsets[:-1]).to(torch.int64)
+    recv_counts = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv_counts, send_counts, group=group)
+    counts = torch.stack([send_counts, recv_counts]).tolist()
+    sc, rc = counts[0], counts[1]
+    recv_rows = _exchange(rows, rc, sc, group)
+    recv_meta = _exchange(meta, rc, sc, group)
+    if recv_rows.shape[0]:
+        y = local_fn(recv_rows, recv_meta[:, 0:1], recv_meta[:, 1:2].view(torch.float32))
+    else:
+        y = recv_rows.new_empty((0, H))
+    back = _exchange(y, sc, rc, group)
+    return ops._ep_combine_impl(back, inv, k)
+
+
 def local_packed_fn(packed, impl: int) -> LocalFn:
     """The local experts through the B200 kernels, as a top-1 layer."""
     from . import ops
 
     def fn(rows: torch.Tensor, local_ids: torch.Tensor, routed_w: torch.Tensor) -> torch.Tensor:
-        return ops.fused_moe_packed(rows, packed.qw1, packed.sw1, packed.qw2, packed.sw2,
-                                    routed_w.view(-1, 1), local_ids.view(-1, 1), packed.bits, impl)
+        return ops._fused_moe_packed_impl(rows, packed.qw1, packed.sw1, packed.qw2, packed.sw2,
+                                          routed_w.reshape(-1, 1), local_ids.reshape(-1, 1), packed.bits, impl)
     return fn
 
 
@@ -99,6 +118,6 @@ def ep_moe_layer(x: torch.Tensor, gate_w: torch.Tensor, packed, top_k: int, rank
                  group=None) -> torch.Tensor:
     """One expert-parallel MoE layer on this rank's tokens ``x`` [T_r, H]."""
     from . import ops
-    topk_w, topk_ids, _ = ops.route(x, gate_w, top_k, bias, renormalize)
+    topk_w, topk_ids, _ = ops._route_impl(x, gate_w, top_k, bias, renormalize)
     return ep_dispatch_combine(x, topk_w, topk_ids, packed.num_experts, local_packed_fn(packed, impl),
                                group=group)

@@ -77,6 +77,7 @@ def moe_layer(x: torch.Tensor, gate_w: torch.Tensor, packed: PackedExperts, top_
               impl: str = "auto") -> torch.Tensor:
     """Router + routed experts, the forward of a PACKED LLaDA MoE block: one router
     kernel (bf16 logits, fp32 softmax, top-k) then :func:`fused_moe`."""
-    topk_w, topk_ids, _ = ops.route(x, gate_w, top_k, bias, renormalize)
-    return ops.fused_moe_packed(x, packed.qw1, packed.sw1, packed.qw2, packed.sw2, topk_w,
-                                topk_ids, packed.bits, IMPL[impl])
+    # eager hot path: the op implementations directly (no per-call dispatcher cost)
+    topk_w, topk_ids, _ = ops._route_impl(x, gate_w, top_k, bias, renormalize)
+    return ops._fused_moe_packed_impl(x, packed.qw1, packed.sw1, packed.qw2, packed.sw2, topk_w,
+                                      topk_ids, packed.bits, IMPL[impl])

@@ -3,6 +3,11 @@
 Each op takes CUDA tensors, launches on the current stream and never
 synchronizes the host.  Fake (meta) implementations give output shapes for
 tracing.  There is no CPU implementation: a CPU tensor raises.
+
+Every op ``name`` is a ``torch.library`` custom op wrapping the plain function
+``_name_impl``; latency-critical eager callers (the expert-parallel layer,
+the whole-layer helpers) call ``_name_impl`` directly and skip the
+dispatcher's per-call host cost (tens of microseconds).
 """
 
 from __future__ import annotations
@@ -45,8 +50,7 @@ def effective_groups(K: int, group_size: int) -> Tuple[int, int]:
 # ---------------------------------------------------------------------------
 
 
-@torch.library.custom_op("llada_quant::quantize_pack", mutates_args=())
-def quantize_pack(w: torch.Tensor, bits: int, group_size: int, scale_search: int, grid: int,
+def _quantize_pack_impl(w: torch.Tensor, bits: int, group_size: int, scale_search: int, grid: int,
                   max_shrink: float, scale_round: int, pack: bool) -> Tuple[torch.Tensor, torch.Tensor]:
     _need_cuda(w)
     w = w.contiguous()
@@ -64,6 +68,9 @@ def quantize_pack(w: torch.Tensor, bits: int, group_size: int, scale_search: int
     return q, scale
 
 
+quantize_pack = torch.library.custom_op("llada_quant::quantize_pack", mutates_args=())(_quantize_pack_impl)
+
+
 @quantize_pack.register_fake
 def _(w, bits, group_size, scale_search, grid, max_shrink, scale_round, pack):
     K = w.shape[-1]
@@ -73,8 +80,7 @@ def _(w, bits, group_size, scale_search, grid, max_shrink, scale_round, pack):
             w.new_empty(*w.shape[:-1], groups, dtype=torch.float32))
 
 
-@torch.library.custom_op("llada_quant::search_errors", mutates_args=())
-def search_errors(w: torch.Tensor, bits: int, group_size: int, grid: int,
+def _search_errors_impl(w: torch.Tensor, bits: int, group_size: int, grid: int,
                   max_shrink: float) -> torch.Tensor:
     _need_cuda(w)
     w = w.contiguous()
@@ -89,14 +95,16 @@ def search_errors(w: torch.Tensor, bits: int, group_size: int, grid: int,
     return errs
 
 
+search_errors = torch.library.custom_op("llada_quant::search_errors", mutates_args=())(_search_errors_impl)
+
+
 @search_errors.register_fake
 def _(w, bits, group_size, grid, max_shrink):
     _, groups = effective_groups(w.shape[-1], group_size)
     return w.new_empty(*w.shape[:-1], groups, grid, dtype=torch.float32)
 
 
-@torch.library.custom_op("llada_quant::dequantize", mutates_args=())
-def dequantize(q: torch.Tensor, scale: torch.Tensor, bits: int, group_size: int, packed: bool,
+def _dequantize_impl(q: torch.Tensor, scale: torch.Tensor, bits: int, group_size: int, packed: bool,
                dtype: torch.dtype) -> torch.Tensor:
     _need_cuda(q, scale)
     q = q.contiguous()
@@ -109,14 +117,16 @@ def dequantize(q: torch.Tensor, scale: torch.Tensor, bits: int, group_size: int,
     return out
 
 
+dequantize = torch.library.custom_op("llada_quant::dequantize", mutates_args=())(_dequantize_impl)
+
+
 @dequantize.register_fake
 def _(q, scale, bits, group_size, packed, dtype):
     K = q.shape[-1] * (2 if packed else 1)
     return q.new_empty(*q.shape[:-1], K, dtype=dtype)
 
 
-@torch.library.custom_op("llada_quant::pack_int4", mutates_args=())
-def pack_int4(values: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+def _pack_int4_impl(values: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     """Returns (packed, range_error) -- range_error is a device int32 flag (1 = out of [-8, 7])."""
     _need_cuda(values)
     values = values.contiguous()
@@ -127,20 +137,25 @@ def pack_int4(values: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     return out, flag
 
 
+pack_int4 = torch.library.custom_op("llada_quant::pack_int4", mutates_args=())(_pack_int4_impl)
+
+
 @pack_int4.register_fake
 def _(values):
     return (values.new_empty(*values.shape[:-1], values.shape[-1] // 2, dtype=torch.int8),
             values.new_empty(1, dtype=torch.int32))
 
 
-@torch.library.custom_op("llada_quant::unpack_int4", mutates_args=())
-def unpack_int4(packed: torch.Tensor) -> torch.Tensor:
+def _unpack_int4_impl(packed: torch.Tensor) -> torch.Tensor:
     _need_cuda(packed)
     packed = packed.contiguous()
     out = torch.empty(*packed.shape[:-1], packed.shape[-1] * 2, dtype=torch.int8, device=packed.device)
     check(load().llq_unpack_int4(packed.data_ptr(), packed.numel() * 2, out.data_ptr(),
                                  _stream(packed)), "unpack_int4")
     return out
+
+
+unpack_int4 = torch.library.custom_op("llada_quant::unpack_int4", mutates_args=())(_unpack_int4_impl)
 
 
 @unpack_int4.register_fake
@@ -153,8 +168,7 @@ def _(packed):
 # ---------------------------------------------------------------------------
 
 
-@torch.library.custom_op("llada_quant::route", mutates_args=())
-def route(x: torch.Tensor, gate_w: torch.Tensor, k: int, bias: Optional[torch.Tensor],
+def _route_impl(x: torch.Tensor, gate_w: torch.Tensor, k: int, bias: Optional[torch.Tensor],
           renormalize: bool) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """bf16 router logits, fp32 softmax, top-k -> (topk_w f32 [T,k], topk_ids i32 [T,k], logits bf16 [T,E])."""
     _need_cuda(x, gate_w, bias)
@@ -171,6 +185,9 @@ def route(x: torch.Tensor, gate_w: torch.Tensor, k: int, bias: Optional[torch.Te
     return w, ids, logits
 
 
+route = torch.library.custom_op("llada_quant::route", mutates_args=())(_route_impl)
+
+
 @route.register_fake
 def _(x, gate_w, k, bias, renormalize):
     T, E = x.shape[0], gate_w.shape[0]
@@ -178,8 +195,7 @@ def _(x, gate_w, k, bias, renormalize):
             x.new_empty(T, E, dtype=torch.bfloat16))
 
 
-@torch.library.custom_op("llada_quant::route_topk", mutates_args=())
-def route_topk(logits: torch.Tensor, k: int, bias: Optional[torch.Tensor],
+def _route_topk_impl(logits: torch.Tensor, k: int, bias: Optional[torch.Tensor],
                renormalize: bool) -> Tuple[torch.Tensor, torch.Tensor]:
     _need_cuda(logits, bias)
     logits = logits.contiguous()
@@ -195,14 +211,16 @@ def route_topk(logits: torch.Tensor, k: int, bias: Optional[torch.Tensor],
     return w, ids
 
 
+route_topk = torch.library.custom_op("llada_quant::route_topk", mutates_args=())(_route_topk_impl)
+
+
 @route_topk.register_fake
 def _(logits, k, bias, renormalize):
     T = logits.shape[0]
     return logits.new_empty(T, k, dtype=torch.float32), logits.new_empty(T, k, dtype=torch.int32)
 
 
-@torch.library.custom_op("llada_quant::moe_align", mutates_args=())
-def moe_align(topk_ids: torch.Tensor, num_experts: int) -> Tuple[torch.Tensor, torch.Tensor]:
+def _moe_align_impl(topk_ids: torch.Tensor, num_experts: int) -> Tuple[torch.Tensor, torch.Tensor]:
     """-> (expert_offsets i32 [E+1], sorted_slots i32 [T*k])."""
     _need_cuda(topk_ids)
     ids = topk_ids.contiguous().to(torch.int32)
@@ -217,6 +235,9 @@ def moe_align(topk_ids: torch.Tensor, num_experts: int) -> Tuple[torch.Tensor, t
     return offsets, slots
 
 
+moe_align = torch.library.custom_op("llada_quant::moe_align", mutates_args=())(_moe_align_impl)
+
+
 @moe_align.register_fake
 def _(topk_ids, num_experts):
     T, k = topk_ids.shape
@@ -224,8 +245,7 @@ def _(topk_ids, num_experts):
             topk_ids.new_empty(T * k, dtype=torch.int32))
 
 
-@torch.library.custom_op("llada_quant::moe_permute", mutates_args=())
-def moe_permute(x: torch.Tensor, sorted_slots: torch.Tensor, k: int, kperm: bool = False) -> torch.Tensor:
+def _moe_permute_impl(x: torch.Tensor, sorted_slots: torch.Tensor, k: int, kperm: bool = False) -> torch.Tensor:
     """Rows of ``x`` in expert order; ``kperm`` also applies the fast-mode K order."""
     _need_cuda(x, sorted_slots)
     x = x.contiguous()
@@ -236,13 +256,15 @@ def moe_permute(x: torch.Tensor, sorted_slots: torch.Tensor, k: int, kperm: bool
     return out
 
 
+moe_permute = torch.library.custom_op("llada_quant::moe_permute", mutates_args=())(_moe_permute_impl)
+
+
 @moe_permute.register_fake
 def _(x, sorted_slots, k, kperm=False):
     return x.new_empty(sorted_slots.shape[0], x.shape[1])
 
 
-@torch.library.custom_op("llada_quant::moe_combine", mutates_args=())
-def moe_combine(y_slots: torch.Tensor, k: int) -> torch.Tensor:
+def _moe_combine_impl(y_slots: torch.Tensor, k: int) -> torch.Tensor:
     _need_cuda(y_slots)
     y_slots = y_slots.contiguous()
     n, H = y_slots.shape
@@ -253,9 +275,61 @@ def moe_combine(y_slots: torch.Tensor, k: int) -> torch.Tensor:
     return out
 
 
+moe_combine = torch.library.custom_op("llada_quant::moe_combine", mutates_args=())(_moe_combine_impl)
+
+
 @moe_combine.register_fake
 def _(y_slots, k):
     return y_slots.new_empty(y_slots.shape[0] // k, y_slots.shape[1], dtype=torch.bfloat16)
+
+
+def _ep_pack_impl(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, sorted_slots: torch.Tensor,
+            experts_per_rank: int) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Expert-parallel send buffers: (rows [T*k, H], local expert ids, routed weights, inverse positions)."""
+    _need_cuda(x, topk_ids, topk_w, sorted_slots)
+    x = x.contiguous()
+    T, H = x.shape
+    k = topk_ids.shape[1]
+    ids = topk_ids.contiguous().to(torch.int32)
+    w = topk_w.contiguous().to(torch.float32)
+    n = T * k
+    rows = torch.empty(n, H, dtype=x.dtype, device=x.device)
+    lid = torch.empty(n, dtype=torch.int32, device=x.device)
+    wts = torch.empty(n, dtype=torch.float32, device=x.device)
+    inv = torch.empty(n, dtype=torch.int32, device=x.device)
+    check(load().llq_ep_pack(x.data_ptr(), ids.data_ptr(), w.data_ptr(), T, k, H, experts_per_rank,
+                             sorted_slots.data_ptr(), rows.data_ptr(), lid.data_ptr(), wts.data_ptr(),
+                             inv.data_ptr(), _stream(x)), "ep_pack")
+    return rows, lid, wts, inv
+
+
+ep_pack = torch.library.custom_op("llada_quant::ep_pack", mutates_args=())(_ep_pack_impl)
+
+
+@ep_pack.register_fake
+def _(x, topk_ids, topk_w, sorted_slots, experts_per_rank):
+    n = topk_ids.numel()
+    return (x.new_empty(n, x.shape[1]), x.new_empty(n, dtype=torch.int32), x.new_empty(n, dtype=torch.float32),
+            x.new_empty(n, dtype=torch.int32))
+
+
+def _ep_combine_impl(back: torch.Tensor, inv_pos: torch.Tensor, k: int) -> torch.Tensor:
+    _need_cuda(back, inv_pos)
+    back = back.contiguous()
+    n, H = back.shape
+    T = inv_pos.numel() // k
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=back.device)
+    check(load().llq_ep_combine(back.data_ptr(), inv_pos.data_ptr(), T, k, H, out.data_ptr(), _stream(back)),
+          "ep_combine")
+    return out
+
+
+ep_combine = torch.library.custom_op("llada_quant::ep_combine", mutates_args=())(_ep_combine_impl)
+
+
+@ep_combine.register_fake
+def _(back, inv_pos, k):
+    return back.new_empty(inv_pos.numel() // k, back.shape[1], dtype=torch.bfloat16)
 
 
 # ---------------------------------------------------------------------------
@@ -269,8 +343,7 @@ def _group_of(q: torch.Tensor, scale: torch.Tensor, bits: int) -> int:
     return -1 if g <= 1 else K // g
 
 
-@torch.library.custom_op("llada_quant::moe_gemm1", mutates_args=())
-def moe_gemm1(x_sorted: torch.Tensor, expert_offsets: torch.Tensor, qw1: torch.Tensor,
+def _moe_gemm1_impl(x_sorted: torch.Tensor, expert_offsets: torch.Tensor, qw1: torch.Tensor,
               sw1: torch.Tensor, bits: int, impl: int) -> torch.Tensor:
     _need_cuda(x_sorted, expert_offsets, qw1, sw1)
     E, two_i = qw1.shape[0], qw1.shape[1]
@@ -284,13 +357,15 @@ def moe_gemm1(x_sorted: torch.Tensor, expert_offsets: torch.Tensor, qw1: torch.T
     return h
 
 
+moe_gemm1 = torch.library.custom_op("llada_quant::moe_gemm1", mutates_args=())(_moe_gemm1_impl)
+
+
 @moe_gemm1.register_fake
 def _(x_sorted, expert_offsets, qw1, sw1, bits, impl):
     return x_sorted.new_empty(x_sorted.shape[0], qw1.shape[1] // 2, dtype=torch.bfloat16)
 
 
-@torch.library.custom_op("llada_quant::moe_gemm2", mutates_args=())
-def moe_gemm2(h_sorted: torch.Tensor, expert_offsets: torch.Tensor, sorted_slots: torch.Tensor,
+def _moe_gemm2_impl(h_sorted: torch.Tensor, expert_offsets: torch.Tensor, sorted_slots: torch.Tensor,
               topk_w: torch.Tensor, qw2: torch.Tensor, sw2: torch.Tensor, bits: int,
               impl: int) -> torch.Tensor:
     _need_cuda(h_sorted, expert_offsets, sorted_slots, topk_w, qw2, sw2)
@@ -304,6 +379,9 @@ def moe_gemm2(h_sorted: torch.Tensor, expert_offsets: torch.Tensor, sorted_slots
                                _group_of(qw2, sw2, bits), y.data_ptr(), impl, _stream(h_sorted)),
           "moe_gemm2")
     return y
+
+
+moe_gemm2 = torch.library.custom_op("llada_quant::moe_gemm2", mutates_args=())(_moe_gemm2_impl)
 
 
 @moe_gemm2.register_fake
@@ -325,8 +403,7 @@ def moe_workspace(T: int, k: int, E: int, H: int, I: int, device) -> torch.Tenso
     return ws
 
 
-@torch.library.custom_op("llada_quant::fused_moe_packed", mutates_args=())
-def fused_moe_packed(x: torch.Tensor, qw1: torch.Tensor, sw1: torch.Tensor, qw2: torch.Tensor,
+def _fused_moe_packed_impl(x: torch.Tensor, qw1: torch.Tensor, sw1: torch.Tensor, qw2: torch.Tensor,
                      sw2: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor, bits: int,
                      impl: int) -> torch.Tensor:
     """Routed MoE layer on PACKED weights: align, permute, GEMM1(+SiLU), GEMM2(+weight), combine."""
@@ -351,6 +428,9 @@ def fused_moe_packed(x: torch.Tensor, qw1: torch.Tensor, sw1: torch.Tensor, qw2:
                                       k, bits, g, out.data_ptr(), ws.data_ptr(), ws.numel(), impl,
                                       _stream(x)), "fused_moe_packed")
     return out
+
+
+fused_moe_packed = torch.library.custom_op("llada_quant::fused_moe_packed", mutates_args=())(_fused_moe_packed_impl)
 
 
 @fused_moe_packed.register_fake

@@ -111,3 +111,29 @@ def test_permute_kperm_reorders_each_8_block():
     order = torch.tensor([0, 4, 1, 5, 2, 6, 3, 7])
     idx = (torch.arange(H) // 8) * 8 + order.repeat(H // 8)
     assert torch.equal(perm, plain[:, idx])
+
+
+def test_ep_pack_and_combine_exact():
+    """Expert-parallel pack (rows, local ids, weights, inverse positions) and combine."""
+    from llada_quant_b200 import ops
+    T, H, E, k, world = 40, 256, 16, 4, 4
+    epr = E // world
+    tw, ids = random_routing(T, E, k, seed=7)
+    x = torch.randn(T, H).to(torch.bfloat16)
+    dest = torch.from_numpy(ids // epr).cuda()
+    offsets, order = ops.moe_align(dest, world)
+    rows, lid, wts, inv = ops.ep_pack(x.cuda(), torch.from_numpy(ids).cuda(), torch.from_numpy(tw).cuda(),
+                                      order, epr)
+    o = to_np(order).astype(np.int64)
+    assert np.array_equal(to_np(offsets), np.concatenate([[0], np.cumsum(np.bincount(ids.reshape(-1) // epr, minlength=world))]))
+    assert torch.equal(rows.cpu(), x[torch.from_numpy(o // k)])
+    assert np.array_equal(to_np(lid), ids.reshape(-1)[o] % epr)
+    assert np.array_equal(to_np(wts), tw.reshape(-1)[o])
+    assert np.array_equal(to_np(inv)[o], np.arange(T * k))
+    back = torch.randn(T * k, H).to(torch.bfloat16)
+    out = ops.ep_combine(back.cuda(), inv, k)
+    b = to_np(back)
+    ref = np.zeros((T, H), np.float32)
+    for j in range(k):
+        ref = (ref + b[to_np(inv).reshape(T, k)[:, j]]).astype(np.float32)
+    assert np.array_equal(to_np(out), S.round_to_bf16(ref))
