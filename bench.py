@@ -10,8 +10,14 @@ bf16 quantized by this package's pack kernel, x ~ N(0,1) bf16, router N(0,0.02).
 Steps rotate over 4 distinct layer weight sets (855 MB > the 126 MB L2), so no
 step reads weights left in L2 by the previous one.
 
-At N > 1 the layer runs expert-parallel (experts sharded contiguously, NCCL
-all-to-all dispatch/combine), T=256 tokens per rank (weak scaling).
+At N > 1 the layer runs expert-parallel (experts sharded contiguously), T=256
+tokens per rank (weak scaling); rows travel by peer-memory stores through each
+rank's exchange window (``--ep-transport window``, the default) or by NCCL
+all-to-alls (``--ep-transport nccl``).
+
+At N = 1 the line also carries ``gpu_reference``: the reference's own PACKED
+algorithm on the same B200 -- dequantize every expert to BF16 (the property's
+fresh tensor per access) and a routed BF16 grouped matmul -- in torch ops.
 
 ``--impl reference`` times the reference's CPU path (the numpy port of
 dequantize_tensor + the routed dequant-then-matmul, oracle/moe.py) on the host
@@ -212,6 +218,97 @@ def make_layers(device, n_layers: int, E_local: int, e0: int):
     return layers, gate_w
 
 
+def _ref_dequantize(q, s, bits: int):
+    """The reference's dequantize_tensor on PACKED buffers (symmetric.py:272-293, unpack_int4
+    :316-346) in torch ops: sign-extend both nibbles, fp32 q * scale per group, cast to bf16."""
+    import torch
+    if bits == 4:
+        lo = torch.bitwise_right_shift(torch.bitwise_left_shift(q, 4), 4)
+        hi = torch.bitwise_right_shift(q, 4)
+        v = torch.stack([lo, hi], dim=-1).reshape(*q.shape[:-1], q.shape[-1] * 2)
+    else:
+        v = q
+    g = s.shape[-1]
+    K = v.shape[-1]
+    w = v.float().reshape(*v.shape[:-1], g, K // g) * s.float().unsqueeze(-1)
+    return w.reshape(v.shape).to(torch.bfloat16)
+
+
+def _ref_layer(x, gate_w, layer, grouped: bool):
+    """The reference PACKED forward on the GPU: block.w1/w2 dequantized afresh (runtime/moe.py:
+    199-216), router softmax(fp32).topk (trajectory/llada.py:225-234), and the routed FFN in
+    the fused_moe rounding order (INFERENCE_REPO_CHANGES.md:259-265, 296-309) as BF16
+    matmuls (torch._grouped_mm, or one matmul per expert)."""
+    import torch
+    import torch.nn.functional as F
+    W1 = _ref_dequantize(layer.qw1, layer.sw1, BITS)
+    W2 = _ref_dequantize(layer.qw2, layer.sw2, BITS)
+    probs = F.softmax(F.linear(x, gate_w), dim=-1, dtype=torch.float32)
+    tw, ti = probs.topk(TOPK, dim=-1)
+    flat = ti.reshape(-1)
+    order = torch.argsort(flat, stable=True)
+    counts = torch.bincount(flat, minlength=E)
+    xs = x.index_select(0, order // TOPK)
+    if grouped:
+        offs = torch.cumsum(counts, 0).to(torch.int32)
+        a = torch._grouped_mm(xs, W1.transpose(1, 2), offs=offs)
+    else:
+        a = torch.empty(xs.shape[0], 2 * I, dtype=torch.bfloat16, device=x.device)
+        c = counts.tolist()
+        o = 0
+        for e in range(E):
+            if c[e]:
+                a[o:o + c[e]] = xs[o:o + c[e]] @ W1[e].t()
+            o += c[e]
+    gt, up = a[:, :I].float(), a[:, I:].float()
+    h = ((gt / (1.0 + torch.exp(-gt))).to(torch.bfloat16).float() * up).to(torch.bfloat16)
+    if grouped:
+        y = torch._grouped_mm(h, W2.transpose(1, 2), offs=offs, out_dtype=torch.float32)
+    else:
+        y = torch.empty(h.shape[0], H, dtype=torch.float32, device=x.device)
+        o = 0
+        for e in range(E):
+            if c[e]:
+                y[o:o + c[e]] = (h[o:o + c[e]] @ W2[e].t()).float()
+            o += c[e]
+    y = (y * tw.reshape(-1)[order].unsqueeze(1)).to(torch.bfloat16)
+    slots = torch.empty_like(y)
+    slots[order] = y
+    return slots.view(-1, TOPK, H).float().sum(dim=1).to(torch.bfloat16)
+
+
+def time_gpu_reference(xs, gate_w, layers, args, device):
+    """The reference algorithm on the same B200, timed like our device value."""
+    import torch
+    grouped = True
+    try:
+        _ref_layer(xs[0], gate_w, layers[0], True)
+        torch.cuda.synchronize()
+    except Exception:
+        grouped = False
+    for i in range(max(2, min(args.warmup, 3))):
+        _ref_layer(xs[i % N_LAYERS], gate_w, layers[i % N_LAYERS], grouped)
+    torch.cuda.synchronize()
+    steps = max(3, min(args.steps, 10))
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(steps):
+        _ref_layer(xs[i % N_LAYERS], gate_w, layers[i % N_LAYERS], grouped)
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    from llada_quant_b200 import ops
+    ref = _ref_layer(xs[0], gate_w, layers[0], grouped).float()
+    tw, ids, _ = ops._route_impl(xs[0], gate_w, TOPK, None, False)
+    ours = ops._fused_moe_packed_impl(xs[0], layers[0].qw1, layers[0].sw1, layers[0].qw2, layers[0].sw2, tw, ids,
+                                      BITS, 0).float()
+    rel = float((ours - ref).norm() / ref.norm())
+    return {"value": T_PER_RANK / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "steps": steps,
+            "rel_l2_vs_ours": rel,
+            "method": "reference PACKED path on this GPU: dequantize_tensor of w1/w2 to bf16 per call + "
+                      + ("torch._grouped_mm" if grouped else "per-expert torch matmul") + " (bf16)"}
+
+
 def run_ours(args, rank: int, world: int, local_rank: int):
     import torch
     import torch.distributed as dist
@@ -232,12 +329,15 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     g = torch.Generator(device=device).manual_seed(2 + rank)
     xs = [torch.randn(T_PER_RANK, H, generator=g, device=device).to(torch.bfloat16) for _ in range(N_LAYERS)]
     bias = None
+    window = None
+    if world > 1 and args.ep_transport == "window":
+        window = ep.EPWindow(T_PER_RANK, TOPK, H, rank, world, device)
 
     def step(i):
         layer = layers[i % N_LAYERS]
         x = xs[i % N_LAYERS]
         if world > 1:
-            return ep.ep_moe_layer(x, gate_w, layer, TOPK, rank, world, bias=bias, impl=impl)
+            return ep.ep_moe_layer(x, gate_w, layer, TOPK, rank, world, bias=bias, impl=impl, window=window)
         tw, ids, _ = ops._route_impl(x, gate_w, TOPK, bias, False)
         return ops._fused_moe_packed_impl(x, layer.qw1, layer.sw1, layer.qw2, layer.sw2, tw, ids, BITS, impl)
 
@@ -277,7 +377,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         x = x_host[i % N_LAYERS].to(device, non_blocking=True)
         if world > 1:
             from llada_quant_b200 import ep
-            out = ep.ep_moe_layer(x, gate_w, layers[i % N_LAYERS], TOPK, rank, world, impl=impl)
+            out = ep.ep_moe_layer(x, gate_w, layers[i % N_LAYERS], TOPK, rank, world, impl=impl, window=window)
         else:
             out = moe_layer(x, gate_w, layers[i % N_LAYERS], TOPK, impl=args.gemm)
         out_host.copy_(out, non_blocking=True)
@@ -336,15 +436,20 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         kernel["layer"] = {"algorithmic_bytes": layer_algo, "achieved": round(layer_gbs, 1),
                            "frac": round(layer_gbs / peak, 4)}
 
+    gpu_ref = None
+    if world == 1 and not args.no_gpu_ref:
+        gpu_ref = time_gpu_reference(xs, gate_w, layers, args, device)
+
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu:
             v, cores, dt = cpu_reference(1)
             cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
                    "sample": f"one C3 layer call (256 tokens) of the numpy port of the reference CPU path, {dt:.1f} s"}
-        # ours per step: router, align, permute, GEMM1, GEMM2, combine (+ the expert-parallel
-        # grouping, gather and slot combine at N > 1)
-        launches_per_step = 6 if world == 1 else 9
+        # ours per step: router, align, permute, GEMM1, GEMM2, combine; at N > 1 over the
+        # window: router, dispatch, align, permute, GEMM1, GEMM2, combine; over NCCL: router,
+        # rank grouping, pack, align, permute, GEMM1, GEMM2, combine, slot combine
+        launches_per_step = 6 if world == 1 else (7 if window is not None else 9)
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
@@ -353,6 +458,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "config": {"workload": "C3 LLaDA-MoE-7B-A1B layer: E=64 H=2048 I=1024 top-8 W4A16 g128",
                        "tokens_per_rank": T_PER_RANK, "gemm": args.gemm,
                        "parallelism": "ep%d" % world if world > 1 else "single",
+                       "ep_transport": (args.ep_transport if world > 1 else None),
                        "l2": "inputs larger than L2: 4 rotated layer weight sets (4 x 214 MB)"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T_PER_RANK * H * 2,
                     "d2h_bytes_per_step": T_PER_RANK * H * 2},
@@ -361,7 +467,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
         }
+        if gpu_ref is not None:
+            line["gpu_reference"] = gpu_ref
         print(json.dumps(line), flush=True)
+    if window is not None:
+        window.close()
 
 
 C4_TOKENS, C4_LAYERS = 32 * 1024, 16
@@ -461,6 +571,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--gemm", choices=["auto", "tcgen05", "tcgen05_fast", "simt"], default="auto")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-gpu-ref", action="store_true",
+                    help="skip the reference-algorithm-on-B200 leg (dequantize + BF16 matmul)")
+    ap.add_argument("--ep-transport", choices=["window", "nccl"], default="window",
+                    help="expert-parallel row exchange at N > 1")
     ap.add_argument("--workload", choices=["c3", "c4"], default="c3",
                     help="c3: one LLaDA-MoE layer at 256 tokens (default, HBM-bound); c4: the 16-layer "
                          "stack over batch 32 x seq 1024 tokens (tensor-bound)")

@@ -160,6 +160,44 @@ int llq_ep_pack(const void* x, const int32_t* topk_ids, const float* topk_w, int
 int llq_ep_combine(const void* back_rows, const int32_t* inv_pos, int64_t T, int k, int H,
                    void* out, void* stream);
 
+/*
+ * Expert parallelism over NVLink peer memory (new work, like llq_ep_pack; it
+ * is the "ep_dispatch / ep_combine" pair of the custom-op surface, without a
+ * collective library or a host synchronisation on the data path).
+ *
+ * Each rank allocates one exchange window of llq_ep_window_bytes(world, cap, H)
+ * with llq_ipc_alloc, passes the llq_ipc_handle_bytes()-byte handle to its
+ * peers (any host channel), maps theirs with llq_ipc_open, and keeps a device
+ * array `peers[world]` of the window bases (its own at [rank]).  cap = the
+ * most (token, slot) entries one rank sends per call (T*k).  One layer call,
+ * with an epoch that starts at 1 and grows by one per call on every rank:
+ *   llq_ep_dispatch      rows + (local expert id, weight) -> the owners' windows
+ *   llq_ep_experts       wait for every rank's dispatch; local experts; GEMM2
+ *                        stores each result into its source rank's window
+ *   llq_ep_combine_wait  wait for every rank's results; out[t] = sum over slots
+ * Waits are bounded (llq_ep_set_timeout_ms, 5 s by default); when one runs out
+ * the kernel records a code in the device error word and carries on.  A
+ * window serves one stream at a time.  rows_hint: the rows expected on this
+ * rank (T*k for balanced routing; picks the token-tile width).
+ */
+size_t llq_ep_window_bytes(int world, int cap, int H);
+int llq_ep_set_timeout_ms(int ms);
+int llq_ipc_handle_bytes(void);
+int llq_ipc_alloc(size_t bytes, void** ptr, void* handle);
+int llq_ipc_open(const void* handle, void** ptr);
+int llq_ipc_close(void* ptr);
+int llq_ipc_free(void* ptr);
+int llq_ep_dispatch(const void* x, const int32_t* topk_ids, const float* topk_w, int64_t T, int k,
+                    int H, int experts_per_rank, void* window, void* const* peers, int rank,
+                    int world, int cap, uint32_t epoch, int32_t* inv_pos, void* stream);
+size_t llq_ep_experts_workspace_size(int world, int cap, int E_local, int H, int I);
+int llq_ep_experts(void* window, void* const* peers, int rank, int world, int cap, uint32_t epoch,
+                   const int8_t* qw1, const float* sw1, const int8_t* qw2, const float* sw2,
+                   int E_local, int H, int I, int bits, int group_size, int64_t rows_hint,
+                   void* workspace, size_t workspace_bytes, int impl, void* stream);
+int llq_ep_combine_wait(void* window, int rank, int world, int cap, uint32_t epoch,
+                        const int32_t* inv_pos, int64_t T, int k, int H, void* out, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Grouped W4A16 / W8A16 expert GEMMs over the packed buffers.                */
 /* ------------------------------------------------------------------------ */

@@ -45,6 +45,17 @@ SIGNATURES = {
     "llq_moe_workspace_size": (c_size_t, [L, I, I, I, I]),
     "llq_fused_moe_packed": (I, [P, P, P, P, P, P, P, L, I, I, I, I, I, I, P, P, c_size_t, I, P]),
     "llq_fused_moe_packed_noalloc": (I, [P, P, P, P, P, P, P, L, I, I, I, I, I, I, P, I, P]),
+    "llq_ep_window_bytes": (c_size_t, [I, I, I]),
+    "llq_ep_set_timeout_ms": (I, [I]),
+    "llq_ipc_handle_bytes": (I, []),
+    "llq_ipc_alloc": (I, [c_size_t, P, P]),
+    "llq_ipc_open": (I, [P, P]),
+    "llq_ipc_close": (I, [P]),
+    "llq_ipc_free": (I, [P]),
+    "llq_ep_dispatch": (I, [P, P, P, L, I, I, I, P, P, I, I, I, ctypes.c_uint32, P, P]),
+    "llq_ep_experts_workspace_size": (c_size_t, [I, I, I, I, I]),
+    "llq_ep_experts": (I, [P, P, I, I, I, ctypes.c_uint32, P, P, P, P, I, I, I, I, I, L, P, c_size_t, I, P]),
+    "llq_ep_combine_wait": (I, [P, I, I, I, ctypes.c_uint32, P, L, I, I, P, P]),
     "llq_device_error": (I, [P]),
     "llq_clear_device_error": (I, []),
 }

@@ -1,0 +1,40 @@
+// Internal entry points shared between the library's translation units.
+#pragma once
+
+#include "ep_window.cuh"
+
+namespace llq {
+
+int quantize_impl(const void*, int, int64_t, int64_t, int, int, int, int, double, int, int, int8_t*,
+                  float*, float*, cudaStream_t);
+int dequantize_impl(const int8_t*, const float*, int64_t, int64_t, int, int, int, void*, int,
+                    cudaStream_t);
+int pack_int4_impl(const int8_t*, int64_t, int8_t*, int32_t*, cudaStream_t);
+int unpack_int4_impl(const int8_t*, int64_t, int8_t*, cudaStream_t);
+int route_impl(const void*, const void*, int64_t, int, int, int, const float*, int, void*, float*,
+               int32_t*, cudaStream_t);
+int route_topk_impl(const void*, int, int64_t, int, int, const float*, int, float*, int32_t*,
+                    cudaStream_t);
+size_t align_workspace_size(int64_t, int, int);
+int align_impl(const int32_t*, int64_t, int, int, int32_t*, int32_t*, void*, size_t, cudaStream_t);
+int permute_impl(const void*, int64_t, int, int, const int32_t*, void*, cudaStream_t, int,
+                 const int32_t* n_dev = nullptr);
+int combine_impl(const void*, int64_t, int, int, void*, cudaStream_t);
+int ep_pack_impl(const void*, const int32_t*, const float*, int64_t, int, int, int, const int32_t*, void*, int32_t*,
+                 float*, int32_t*, cudaStream_t);
+int ep_combine_impl(const void*, const int32_t*, int64_t, int, int, void*, cudaStream_t);
+int gemm1_simt(const void*, const int32_t*, int, int, int, const int8_t*, const float*, int, int,
+               void*, cudaStream_t);
+int gemm2_simt(const void*, const int32_t*, const int32_t*, const float*, int, int, int,
+               const int8_t*, const float*, int, int, void*, cudaStream_t);
+int gemm1_tc(const void*, const int32_t*, int64_t, int, int, int, const int8_t*, const float*, int,
+             int, void*, bool, cudaStream_t, int64_t rows_hint = -1);
+int gemm2_tc(const void*, const int32_t*, const int32_t*, const float*, int64_t, int, int, int,
+             const int8_t*, const float*, int, int, void*, bool, cudaStream_t, int64_t rows_hint = -1,
+             const EpScatter* ep = nullptr);
+bool tc_supported(int E, int N_out, int K, int bits, int group_size, bool gemm1);
+
+int align_impl_masked(const int32_t*, int64_t, int, int32_t*, int32_t*, void*, size_t, cudaStream_t,
+                      const AlignMask&);
+
+}  // namespace llq

@@ -37,6 +37,7 @@
 #include <cudaTypedefs.h>
 
 #include "llq_common.cuh"
+#include "ep_window.cuh"
 
 namespace llq {
 
@@ -117,6 +118,8 @@ struct TcArgs {
   int groups;      // scales per row
   int debug;       // development switch: 1 = no dequant math, 2 = no MMA, 4 = no TMEM stores,
                    // 8 = no token-tile loads (results are wrong)
+  int ep_on;       // GEMM2 only: scatter rows into the peers' back regions and signal them
+  EpScatter ep;
 };
 
 // ---------------------------------------------------------------------------
@@ -670,7 +673,15 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         } else {
           const int32_t slot = args.sorted_slots[p];
           const float w = args.topk_w[slot];
-          __nv_bfloat16* orow = args.out + static_cast<int64_t>(slot) * args.n_out + item.rb * 2 * ROWS + r;
+          __nv_bfloat16* orow;
+          if (args.ep_on) {
+            const int src = slot / args.ep.L.cap;
+            const int64_t at = static_cast<int64_t>(args.ep.me) * args.ep.L.cap + (slot - src * args.ep.L.cap);
+            orow = reinterpret_cast<__nv_bfloat16*>(args.ep.peers[src] + args.ep.L.back) + at * args.n_out;
+          } else {
+            orow = args.out + static_cast<int64_t>(slot) * args.n_out;
+          }
+          orow += item.rb * 2 * ROWS + r;
           orow[0] = __float2bfloat16_rn(__fmul_rn(a0, w));
           orow[ROWS] = __float2bfloat16_rn(__fmul_rn(a1, w));
         }
@@ -744,11 +755,21 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     }
   }
 
+  if (!GEMM1 && args.ep_on && warp >= FIRST_EPI) __threadfence_system();  // rows stored to peers
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+  if (!GEMM1 && args.ep_on && threadIdx.x == 0) {
+    // last CTA out tells every source rank that its rows are back
+    if (atomicAdd(args.ep.done, 1u) == gridDim.x - 1) {
+      __threadfence_system();
+      for (int d = 0; d < args.ep.L.R; ++d)
+        st_release_sys(ep_sig(args.ep.peers[d], args.ep.L, kEpRflag) + args.ep.me, args.ep.epoch);
+      atomicExch(args.ep.done, 0u);
+    }
   }
 }
 
@@ -786,7 +807,8 @@ int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t 
 template <bool GEMM1, int BITS, bool FAST, int NTM>
 int launch_tc(const void* act, int64_t n_rows, const int32_t* offsets, int E, int K, int rows_total,
               int inter, int n_out, const int8_t* q, const float* scale, int group_size,
-              const int32_t* sorted_slots, const float* topk_w, void* out, cudaStream_t st) {
+              const int32_t* sorted_slots, const float* topk_w, void* out, cudaStream_t st,
+              const EpScatter* ep) {
   using C = Cfg<GEMM1, BITS, FAST, NTM>;
   if (n_rows <= 0) return LLQ_OK;
   CUtensorMap tw, tb[4];
@@ -821,6 +843,8 @@ int launch_tc(const void* act, int64_t n_rows, const int32_t* offsets, int E, in
     return e ? atoi(e) : 0;
   }();
   a.debug = debug_flags;
+  a.ep_on = ep != nullptr;
+  if (ep != nullptr) a.ep = *ep;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(moe_gemm_tc_kernel<GEMM1, BITS, FAST, NTM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -834,15 +858,17 @@ int launch_tc(const void* act, int64_t n_rows, const int32_t* offsets, int E, in
 }
 
 // decode tiles (64 tokens) unless the average expert holds more than 96 rows
+// (rows_hint: the expected number of rows, when n_rows is a capacity)
 template <bool GEMM1, int BITS, bool FAST>
 int launch_any(int64_t n_rows, int E, const void* act, const int32_t* offsets, int K, int rows_total,
                int inter, int n_out, const int8_t* q, const float* scale, int group_size,
-               const int32_t* sorted_slots, const float* topk_w, void* out, cudaStream_t st) {
-  if (!FAST && n_rows > static_cast<int64_t>(E) * 96)
+               const int32_t* sorted_slots, const float* topk_w, void* out, cudaStream_t st,
+               int64_t rows_hint, const EpScatter* ep) {
+  if (!FAST && rows_hint > static_cast<int64_t>(E) * 96)
     return launch_tc<GEMM1, BITS, false, 128>(act, n_rows, offsets, E, K, rows_total, inter, n_out, q, scale,
-                                              group_size, sorted_slots, topk_w, out, st);
+                                              group_size, sorted_slots, topk_w, out, st, ep);
   return launch_tc<GEMM1, BITS, FAST, 64>(act, n_rows, offsets, E, K, rows_total, inter, n_out, q, scale,
-                                          group_size, sorted_slots, topk_w, out, st);
+                                          group_size, sorted_slots, topk_w, out, st, ep);
 }
 
 }  // namespace
@@ -859,36 +885,39 @@ bool tc_supported(int E, int N_out, int K, int bits, int group_size, bool gemm1)
 
 int gemm1_tc(const void* x_sorted, const int32_t* offsets, int64_t n_rows, int E, int H, int I,
              const int8_t* qw1, const float* sw1, int bits, int group_size, void* h_sorted, bool fast,
-             cudaStream_t st) {
+             cudaStream_t st, int64_t rows_hint) {
   if (!tc_supported(E, I, H, bits, group_size, true))
     return fail(LLQ_EUNSUPPORTED, "tcgen05 GEMM1: unsupported shape");
   if (fast && bits != 4) return fail(LLQ_EUNSUPPORTED, "fast dequantization is INT4 only");
+  if (rows_hint < 0) rows_hint = n_rows;
   if (bits == 4) {
     if (fast)
       return launch_any<true, 4, true>(n_rows, E, x_sorted, offsets, H, 2 * I, I, I, qw1, sw1, group_size,
-                                       nullptr, nullptr, h_sorted, st);
+                                       nullptr, nullptr, h_sorted, st, rows_hint, nullptr);
     return launch_any<true, 4, false>(n_rows, E, x_sorted, offsets, H, 2 * I, I, I, qw1, sw1, group_size,
-                                      nullptr, nullptr, h_sorted, st);
+                                      nullptr, nullptr, h_sorted, st, rows_hint, nullptr);
   }
   return launch_any<true, 8, false>(n_rows, E, x_sorted, offsets, H, 2 * I, I, I, qw1, sw1, group_size,
-                                    nullptr, nullptr, h_sorted, st);
+                                    nullptr, nullptr, h_sorted, st, rows_hint, nullptr);
 }
 
 int gemm2_tc(const void* h_sorted, const int32_t* offsets, const int32_t* sorted_slots,
              const float* topk_w, int64_t n_rows, int E, int H, int I, const int8_t* qw2,
-             const float* sw2, int bits, int group_size, void* y_slots, bool fast, cudaStream_t st) {
+             const float* sw2, int bits, int group_size, void* y_slots, bool fast, cudaStream_t st,
+             int64_t rows_hint, const EpScatter* ep) {
   if (!tc_supported(E, H, I, bits, group_size, false))
     return fail(LLQ_EUNSUPPORTED, "tcgen05 GEMM2: unsupported shape");
   if (fast && bits != 4) return fail(LLQ_EUNSUPPORTED, "fast dequantization is INT4 only");
+  if (rows_hint < 0) rows_hint = n_rows;
   if (bits == 4) {
     if (fast)
       return launch_any<false, 4, true>(n_rows, E, h_sorted, offsets, I, H, 0, H, qw2, sw2, group_size,
-                                        sorted_slots, topk_w, y_slots, st);
+                                        sorted_slots, topk_w, y_slots, st, rows_hint, ep);
     return launch_any<false, 4, false>(n_rows, E, h_sorted, offsets, I, H, 0, H, qw2, sw2, group_size,
-                                       sorted_slots, topk_w, y_slots, st);
+                                       sorted_slots, topk_w, y_slots, st, rows_hint, ep);
   }
   return launch_any<false, 8, false>(n_rows, E, h_sorted, offsets, I, H, 0, H, qw2, sw2, group_size,
-                                     sorted_slots, topk_w, y_slots, st);
+                                     sorted_slots, topk_w, y_slots, st, rows_hint, ep);
 }
 
 }  // namespace llq

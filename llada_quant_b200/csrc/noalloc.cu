@@ -22,14 +22,9 @@
 // different host threads -- race on it and corrupt each other's results.
 #include <mutex>
 
-#include "llq_common.cuh"
+#include "llq_internal.cuh"
 
 namespace llq {
-
-int align_impl(const int32_t*, int64_t, int, int, int32_t*, int32_t*, void*, size_t, cudaStream_t);
-size_t align_workspace_size(int64_t, int, int);
-int permute_impl(const void*, int64_t, int, int, const int32_t*, void*, cudaStream_t, int);
-int combine_impl(const void*, int64_t, int, int, void*, cudaStream_t);
 
 namespace {
 

@@ -10,6 +10,7 @@
 // order (the contract of the external moe_align_block_size,
 // INFERENCE_REPO_CHANGES.md:274-278).
 #include "llq_common.cuh"
+#include "ep_window.cuh"
 
 namespace llq {
 
@@ -200,17 +201,27 @@ __global__ void route_topk_kernel(const L* __restrict__ logits, int64_t T, int E
 // ---------------------------------------------------------------------------
 // alignment: count -> scan -> stable scatter
 // ---------------------------------------------------------------------------
+
+__device__ __forceinline__ int mask_count(const AlignMask& m, int r) {
+  const int c = static_cast<int>(ld_acquire_sys(m.counts + r));
+  return c < m.cap ? (c < 0 ? 0 : c) : m.cap;
+}
+
 constexpr int kAlignChunk = 2048;  // (token, slot) entries per block
 constexpr int kAlignThreads = 256;
 
 __global__ void __launch_bounds__(kAlignThreads) align_count_kernel(
-    const int32_t* __restrict__ ids, int64_t n, int E, int32_t* __restrict__ counts) {
+    const int32_t* __restrict__ ids, int64_t n, int E, int32_t* __restrict__ counts, AlignMask m) {
   __shared__ int32_t c[kMaxExperts];
+  __shared__ int32_t vc[kMaxRanks];
   for (int e = threadIdx.x; e < E; e += blockDim.x) c[e] = 0;
+  if (m.counts != nullptr)
+    for (int r = threadIdx.x; r < m.R; r += blockDim.x) vc[r] = mask_count(m, r);
   __syncthreads();
   const int64_t lo = static_cast<int64_t>(blockIdx.x) * kAlignChunk;
   const int64_t hi = lo + kAlignChunk < n ? lo + kAlignChunk : n;
   for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    if (m.counts != nullptr && (i % m.cap) >= vc[i / m.cap]) continue;
     const int e = ids[i];
     if (e >= 0 && e < E) atomicAdd(&c[e], 1);
     else atomicExch(&g_device_error, 2);
@@ -253,8 +264,11 @@ __global__ void __launch_bounds__(kMaxExperts) align_scan_kernel(int32_t* __rest
 
 __global__ void __launch_bounds__(kAlignThreads) align_scatter_kernel(
     const int32_t* __restrict__ ids, int64_t n, int E, const int32_t* __restrict__ base,
-    int32_t* __restrict__ sorted_slots) {
+    int32_t* __restrict__ sorted_slots, AlignMask m) {
   __shared__ int32_t cursor[kMaxExperts];
+  __shared__ int32_t vc[kMaxRanks];
+  if (m.counts != nullptr)
+    for (int r = threadIdx.x; r < m.R; r += blockDim.x) vc[r] = mask_count(m, r);
   __shared__ int32_t wcnt[kAlignThreads / 32][kMaxExperts];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int e = threadIdx.x; e < E; e += blockDim.x) cursor[e] = base[static_cast<int64_t>(blockIdx.x) * E + e];
@@ -267,7 +281,7 @@ __global__ void __launch_bounds__(kAlignThreads) align_scatter_kernel(
   for (int64_t r0 = lo; r0 < hi; r0 += kAlignThreads) {
     const int64_t i = r0 + threadIdx.x;
     int e = -1;
-    if (i < hi) {
+    if (i < hi && (m.counts == nullptr || (i % m.cap) < vc[i / m.cap])) {
       e = ids[i];
       if (e < 0 || e >= E) e = -1;
     }
@@ -303,16 +317,23 @@ constexpr int kAlignSmallThreads = 1024;
 
 __global__ void __launch_bounds__(kAlignSmallThreads) align_small_kernel(
     const int32_t* __restrict__ ids, int n, int E, int32_t* __restrict__ offsets,
-    int32_t* __restrict__ sorted_slots) {
+    int32_t* __restrict__ sorted_slots, AlignMask m) {
   constexpr int W = kAlignSmallThreads / 32;
   __shared__ int32_t cnt[kMaxExperts];
+  __shared__ int32_t vc[kMaxRanks];
   __shared__ int32_t cursor[kMaxExperts];
   __shared__ int32_t wcnt[W][kMaxExperts];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   for (int i = tid; i < kMaxExperts; i += blockDim.x) cnt[i] = 0;
   for (int i = tid; i < W * kMaxExperts; i += blockDim.x) (&wcnt[0][0])[i] = 0;
+  if (m.counts != nullptr) {
+    if (tid == 0 && m.flags != nullptr) ep_wait_flags(m.flags, m.R, m.epoch, m.timeout_ns, 0x501);
+    __syncthreads();
+    for (int r = tid; r < m.R; r += blockDim.x) vc[r] = mask_count(m, r);
+  }
   __syncthreads();
   for (int i = tid; i < n; i += blockDim.x) {
+    if (m.counts != nullptr && (i % m.cap) >= vc[i / m.cap]) continue;
     const int e = ids[i];
     if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
     else atomicExch(&g_device_error, 2);
@@ -350,7 +371,7 @@ __global__ void __launch_bounds__(kAlignSmallThreads) align_small_kernel(
   for (int r0 = 0; r0 < n; r0 += blockDim.x) {
     const int i = r0 + tid;
     int e = -1;
-    if (i < n) {
+    if (i < n && (m.counts == nullptr || (i % m.cap) < vc[i / m.cap])) {
       e = ids[i];
       if (e < 0 || e >= E) e = -1;
     }
@@ -378,8 +399,10 @@ __global__ void __launch_bounds__(kAlignSmallThreads) align_small_kernel(
 
 template <bool KPERM>
 __global__ void permute_kernel(const uint4* __restrict__ x, int64_t n_rows, int vec_per_row, int k,
-                               const int32_t* __restrict__ sorted_slots, uint4* __restrict__ xs) {
-  const int64_t total = n_rows * vec_per_row;
+                               const int32_t* __restrict__ sorted_slots, uint4* __restrict__ xs,
+                               const int32_t* __restrict__ n_dev) {
+  // n_dev (optional): the number of sorted rows, known only on the device
+  const int64_t total = (n_dev != nullptr ? static_cast<int64_t>(*n_dev) : n_rows) * vec_per_row;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t p = i / vec_per_row;
@@ -472,6 +495,10 @@ __global__ void ep_combine_kernel(const uint4* __restrict__ back, const int32_t*
   }
 }
 
+__global__ void ep_wait_kernel(const uint32_t* flags, int R, uint32_t epoch, uint64_t timeout_ns, int code) {
+  if (threadIdx.x == 0) ep_wait_flags(flags, R, epoch, timeout_ns, code);
+}
+
 inline unsigned grid_for(int64_t work, int threads) {
   int64_t b = (work + threads - 1) / threads;
   const int64_t cap = static_cast<int64_t>(num_sms()) * 32;
@@ -526,44 +553,56 @@ size_t align_workspace_size(int64_t T, int k, int E) {
   return static_cast<size_t>((nblk < 1 ? 1 : nblk) * E * sizeof(int32_t) + 256);
 }
 
-int align_impl(const int32_t* ids, int64_t T, int k, int E, int32_t* offsets, int32_t* sorted_slots,
-               void* ws, size_t ws_bytes, cudaStream_t st) {
+int align_impl_masked(const int32_t* ids, int64_t n, int E, int32_t* offsets, int32_t* sorted_slots, void* ws,
+                      size_t ws_bytes, cudaStream_t st, const AlignMask& m) {
   if (E < 1 || E > kMaxExperts) return fail(LLQ_EUNSUPPORTED, "num_experts must be in [1, 256], got %d", E);
-  const int64_t n = T * k;
-  if (ws_bytes < align_workspace_size(T, k, E)) return fail(LLQ_ENOSPACE, "align workspace too small");
+  if (m.counts != nullptr && (m.R < 1 || m.R > kMaxRanks || m.cap < 1))
+    return fail(LLQ_EINVAL, "masked alignment needs 1 <= ranks <= %d and cap >= 1", kMaxRanks);
+  if (ws_bytes < align_workspace_size(n, 1, E)) return fail(LLQ_ENOSPACE, "align workspace too small");
   if (n == 0) {
     cudaMemsetAsync(offsets, 0, sizeof(int32_t) * (E + 1), st);
     return check_launch("align memset");
   }
   if (n <= kAlignSmallMax) {
-    align_small_kernel<<<1, kAlignSmallThreads, 0, st>>>(ids, static_cast<int>(n), E, offsets, sorted_slots);
+    align_small_kernel<<<1, kAlignSmallThreads, 0, st>>>(ids, static_cast<int>(n), E, offsets, sorted_slots, m);
     return check_launch("align_small_kernel");
   }
   const int64_t nblk = (n + kAlignChunk - 1) / kAlignChunk;
   if (nblk > 0x7fffffff) return fail(LLQ_EINVAL, "too many entries");
+  if (m.counts != nullptr && m.flags != nullptr) {
+    ep_wait_kernel<<<1, 32, 0, st>>>(m.flags, m.R, m.epoch, m.timeout_ns, 0x502);
+    int rc = check_launch("ep_wait_kernel");
+    if (rc) return rc;
+  }
   int32_t* counts = static_cast<int32_t*>(ws);
-  align_count_kernel<<<static_cast<unsigned>(nblk), kAlignThreads, 0, st>>>(ids, n, E, counts);
+  align_count_kernel<<<static_cast<unsigned>(nblk), kAlignThreads, 0, st>>>(ids, n, E, counts, m);
   int rc = check_launch("align_count_kernel");
   if (rc) return rc;
   align_scan_kernel<<<1, kMaxExperts, 0, st>>>(counts, static_cast<int>(nblk), E, offsets);
   rc = check_launch("align_scan_kernel");
   if (rc) return rc;
-  align_scatter_kernel<<<static_cast<unsigned>(nblk), kAlignThreads, 0, st>>>(ids, n, E, counts, sorted_slots);
+  align_scatter_kernel<<<static_cast<unsigned>(nblk), kAlignThreads, 0, st>>>(ids, n, E, counts, sorted_slots, m);
   return check_launch("align_scatter_kernel");
 }
 
+int align_impl(const int32_t* ids, int64_t T, int k, int E, int32_t* offsets, int32_t* sorted_slots,
+               void* ws, size_t ws_bytes, cudaStream_t st) {
+  AlignMask m{};
+  return align_impl_masked(ids, T * k, E, offsets, sorted_slots, ws, ws_bytes, st, m);
+}
+
 int permute_impl(const void* x, int64_t T, int H, int k, const int32_t* sorted_slots, void* xs,
-                 cudaStream_t st, int kperm) {
+                 cudaStream_t st, int kperm, const int32_t* n_dev) {
   if (H % 8 != 0) return fail(LLQ_EUNSUPPORTED, "hidden size must be a multiple of 8");
   const int64_t n = T * k;
   if (n == 0) return LLQ_OK;
   const int vpr = H / 8;
   if (kperm)
     permute_kernel<true><<<grid_for(n * vpr, 256), 256, 0, st>>>(static_cast<const uint4*>(x), n, vpr, k,
-                                                                 sorted_slots, static_cast<uint4*>(xs));
+                                                                 sorted_slots, static_cast<uint4*>(xs), n_dev);
   else
     permute_kernel<false><<<grid_for(n * vpr, 256), 256, 0, st>>>(static_cast<const uint4*>(x), n, vpr, k,
-                                                                  sorted_slots, static_cast<uint4*>(xs));
+                                                                  sorted_slots, static_cast<uint4*>(xs), n_dev);
   return check_launch("permute_kernel");
 }
 

@@ -16,14 +16,26 @@ data-parallel.  One layer call on each rank:
 
 Because every (token, slot) result is computed by the same kernels on the
 same row, and the slots are summed in the same order, the output equals the
-single-GPU layer bit for bit.  The collective plumbing is plain
-``torch.distributed`` (backend nccl on GPUs, gloo in the CPU tests, where a
-caller-supplied ``local_fn`` stands in for the kernels).
+single-GPU layer bit for bit.
+
+Two transports carry steps 3 and 5:
+
+* ``EPWindow`` (the GPU default): each rank owns an exchange window mapped
+  into every peer through CUDA IPC; the dispatch kernel stores rows straight
+  into the owners' windows, the expert GEMM2 stores its results straight back
+  into the source ranks' windows, and device flags with epochs replace the
+  host synchronisation (three library calls per layer, no collective on the
+  data path);
+* ``ep_dispatch_combine``: ``torch.distributed`` all-to-alls (nccl on GPUs,
+  gloo in the CPU tests, where a caller-supplied ``local_fn`` stands in for
+  the kernels), with one host read of the split sizes.
 """
 
 from __future__ import annotations
 
 from typing import Callable, Optional
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -115,9 +127,119 @@ def local_packed_fn(packed, impl: int) -> LocalFn:
 
 def ep_moe_layer(x: torch.Tensor, gate_w: torch.Tensor, packed, top_k: int, rank: int, world: int,
                  bias: Optional[torch.Tensor] = None, renormalize: bool = False, impl: int = 0,
-                 group=None) -> torch.Tensor:
-    """One expert-parallel MoE layer on this rank's tokens ``x`` [T_r, H]."""
+                 group=None, window: Optional["EPWindow"] = None) -> torch.Tensor:
+    """One expert-parallel MoE layer on this rank's tokens ``x`` [T_r, H]: over the
+    peer-memory ``window`` when one is given, else over torch.distributed all-to-alls."""
     from . import ops
     topk_w, topk_ids, _ = ops._route_impl(x, gate_w, top_k, bias, renormalize)
+    if window is not None:
+        return window.layer(x, topk_w, topk_ids, packed, impl)
     return ep_dispatch_combine(x, topk_w, topk_ids, packed.num_experts, local_packed_fn(packed, impl),
                                group=group)
+
+
+class EPWindow:
+    """This rank's peer-memory exchange window for expert-parallel layers.
+
+    ``max_tokens``: the most tokens this rank passes to one layer call (the
+    window holds ``max_tokens * top_k`` entries from every rank).  Creating and
+    closing a window are collective over ``group``; the calls in between are
+    not -- ranks only meet through device flags.  One window serves every layer
+    of a model (the calls are ordered on one stream)."""
+
+    def __init__(self, max_tokens: int, top_k: int, hidden: int, rank: int, world: int,
+                 device: torch.device, group=None):
+        from ._lib import check, load
+        lib = load()
+        self.rank, self.world, self.k, self.hidden = rank, world, top_k, hidden
+        self.cap = max(1, max_tokens * top_k)
+        self.device = torch.device(device)
+        self.group = group
+        self.nbytes = lib.llq_ep_window_bytes(world, self.cap, hidden)
+        handle = ctypes.create_string_buffer(lib.llq_ipc_handle_bytes())
+        base = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            check(lib.llq_ipc_alloc(self.nbytes, ctypes.byref(base), handle), "ep window")
+        self.base = base.value
+        self._opened = []
+        bases = [0] * world
+        bases[rank] = self.base
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, handle.raw, group=group)
+            with torch.cuda.device(self.device):
+                for r in range(world):
+                    if r == rank:
+                        continue
+                    p = ctypes.c_void_p()
+                    check(lib.llq_ipc_open(ctypes.create_string_buffer(handles[r], len(handles[r])),
+                                           ctypes.byref(p)), "ep window open")
+                    bases[r] = p.value
+                    self._opened.append(p.value)
+            dist.barrier(group=group)
+        self.peers = torch.tensor(bases, dtype=torch.int64, device=self.device)
+        self.epoch = 0
+        self._ws = None
+
+    def _workspace(self, E: int, I: int) -> torch.Tensor:
+        from ._lib import load
+        n = load().llq_ep_experts_workspace_size(self.world, self.cap, E, self.hidden, I)
+        if self._ws is None or self._ws.numel() < n:
+            self._ws = torch.empty(n, dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def layer(self, x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor, packed, impl: int) -> torch.Tensor:
+        """Steps 2-5 for routed tokens ``x`` [T, H] against this rank's expert shard ``packed``."""
+        from ._lib import check, load
+        from .ops import _group_of, _stream
+        lib = load()
+        T, H = x.shape
+        k = topk_ids.shape[1]
+        if H != self.hidden or T * k > self.cap:
+            raise ValueError(f"window holds {self.cap} entries of hidden size {self.hidden}; "
+                             f"got T*k = {T * k}, H = {H}")
+        x = x.contiguous()
+        ids = topk_ids.contiguous().to(torch.int32)
+        w = topk_w.contiguous().to(torch.float32)
+        E_local, I = packed.num_experts, packed.intermediate
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+        st = _stream(x)
+        inv = torch.empty(T * k, dtype=torch.int32, device=x.device)
+        check(lib.llq_ep_dispatch(x.data_ptr(), ids.data_ptr(), w.data_ptr(), T, k, H, E_local, self.base,
+                                  self.peers.data_ptr(), self.rank, self.world, self.cap, self.epoch,
+                                  inv.data_ptr(), st), "ep_dispatch")
+        ws = self._workspace(E_local, I)
+        check(lib.llq_ep_experts(self.base, self.peers.data_ptr(), self.rank, self.world, self.cap, self.epoch,
+                                 packed.qw1.data_ptr(), packed.sw1.data_ptr(), packed.qw2.data_ptr(),
+                                 packed.sw2.data_ptr(), E_local, H, I, packed.bits,
+                                 _group_of(packed.qw1, packed.sw1, packed.bits), T * k, ws.data_ptr(),
+                                 ws.numel(), impl, st), "ep_experts")
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
+        check(lib.llq_ep_combine_wait(self.base, self.rank, self.world, self.cap, self.epoch, inv.data_ptr(),
+                                      T, k, H, out.data_ptr(), st), "ep_combine")
+        return out
+
+    def close(self) -> None:
+        """Collective: unmap the peers' windows and free this one."""
+        from ._lib import check, load
+        if self.base is None:
+            return
+        lib = load()
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                check(lib.llq_ipc_close(p), "ep window close")
+            self._opened = []
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            check(lib.llq_ipc_free(self.base), "ep window free")
+        self.base = None
+
+
+def set_wait_timeout_ms(ms: int) -> None:
+    """Bound of every cross-GPU wait of the peer-memory path (default 5000 ms)."""
+    from ._lib import check, load
+    check(load().llq_ep_set_timeout_ms(int(ms)), "ep timeout")
