@@ -196,3 +196,39 @@ def test_block_packed_mode_end_to_end():
                               to_np(tw), to_np(ids).astype(np.int32), 4)
     _assert_layer_close(to_np(out2), ref2)
     assert M.rel_l2(to_np(out), out_ref) < 0.05
+
+
+def _kperm_pos(n: np.ndarray) -> np.ndarray:
+    j = n & 7
+    return (n & ~7) | np.where(j < 4, 2 * j, 2 * (j - 4) + 1)
+
+
+@pytest.mark.parametrize("impl", IMPLS)
+@pytest.mark.parametrize("bits", [4, 8])
+def test_gemm2_one_hot_rows_read_back_the_dequantized_weights(impl, bits):
+    """With one-hot activation rows and routed weight 1, GEMM2 returns single weights:
+    y[e*I + k, n] = bf16(q[e,n,k] * s) -- the in-register dequantization must equal
+    dequantize_tensor bit for bit, for every nibble position and over group
+    magnitudes from 1e-30 to 1."""
+    from llada_quant_b200 import ops
+    from llada_quant_b200 import symmetric as G
+    code = _impl_or_skip(impl, bits)
+    E, H, I = 2, 256, 1024
+    rng = np.random.default_rng(11)
+    mag = 10.0 ** rng.uniform(-30, 0, size=(E, H, I // 128, 1))
+    w = (rng.standard_normal((E, H, I // 128, 128)) * mag).reshape(E, H, I).astype(np.float32)
+    w2 = torch.from_numpy(w).to(torch.bfloat16)
+    r2 = G.quantize_tensor(w2.cuda(), bits=bits, group_size=128)
+    n = E * I
+    cols = np.tile(np.arange(I), E)
+    if impl == "tcgen05_fast":
+        cols = _kperm_pos(cols)
+    h = torch.zeros(n, I, dtype=torch.bfloat16)
+    h[torch.arange(n), torch.from_numpy(cols)] = 1.0
+    offsets = torch.tensor([0, I, 2 * I], dtype=torch.int32).cuda()
+    slots = torch.arange(n, dtype=torch.int32).cuda()
+    y = ops.moe_gemm2(h.cuda(), offsets, slots, torch.ones(n).cuda(), r2.q, r2.scale, bits, code)
+    ref = S.dequantize_tensor(to_np(r2.q), to_np(r2.scale), bits, 128, packed=bits == 4, to_bf16=True)
+    ref = np.ascontiguousarray(ref.transpose(0, 2, 1)).reshape(n, H)
+    got = to_np(y)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), np.argwhere(got != ref)[:5]
