@@ -9,6 +9,8 @@
 // Alignment groups the T*k (token, slot) entries by expert, stable in entry
 // order (the contract of the external moe_align_block_size,
 // INFERENCE_REPO_CHANGES.md:274-278).
+#include <cstdlib>
+
 #include "llq_common.cuh"
 #include "ep_window.cuh"
 
@@ -17,7 +19,6 @@ namespace llq {
 namespace {
 
 constexpr int kMaxExperts = 256;
-constexpr int kRouteTokens = 4;  // tokens per block in the fused router
 
 // softmax + top-k of one token held by one warp: value j of the lane is
 // expert lane + 32 j
@@ -83,41 +84,53 @@ __device__ void warp_softmax_topk(float (&v)[kMaxExperts / 32], int E, int k, in
   }
 }
 
-// logits + softmax + top-k for kRouteTokens tokens per block.
-__global__ void __launch_bounds__(512) route_kernel(const __nv_bfloat16* __restrict__ x,
-                                                    const __nv_bfloat16* __restrict__ gate_w,
-                                                    int64_t T, int H, int E, int k,
-                                                    const float* __restrict__ bias, int renormalize,
-                                                    __nv_bfloat16* __restrict__ logits_out,
-                                                    float* __restrict__ topk_w,
-                                                    int32_t* __restrict__ topk_ids) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);        // [kRouteTokens][H]
-  float* lg = reinterpret_cast<float*>(xs + kRouteTokens * static_cast<int64_t>(H));  // [kRouteTokens][E]
-  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kRouteTokens;
-  const int nt = static_cast<int>(T - t0 < kRouteTokens ? T - t0 : kRouteTokens);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// logits + softmax + top-k for TOK tokens per block of 256 threads.  Token
+// rows are staged in shared memory as fp32; each warp owns experts
+// warp, warp + 8, ...; lane l sums the 16-byte weight vectors l, l + 32, ...
+// of an expert (every load of a pass issued before any is consumed), then a
+// butterfly sum -- the same order for every TOK, so the logits do not depend
+// on how tokens are grouped into blocks.
+constexpr int kRouteThreads = 256;
 
-  // stage the token rows (16-byte vectors; H % 8 == 0 checked on the host)
+template <int TOK>
+__global__ void __launch_bounds__(kRouteThreads) route_kernel(const __nv_bfloat16* __restrict__ x,
+                                                              const __nv_bfloat16* __restrict__ gate_w,
+                                                              int64_t T, int H, int E, int k,
+                                                              const float* __restrict__ bias, int renormalize,
+                                                              __nv_bfloat16* __restrict__ logits_out,
+                                                              float* __restrict__ topk_w,
+                                                              int32_t* __restrict__ topk_ids) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* xs = reinterpret_cast<float*>(smem_raw);                        // [TOK][H]
+  float* lg = xs + TOK * static_cast<int64_t>(H);                        // [TOK][E]
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * TOK;
+  const int nt = static_cast<int>(T - t0 < TOK ? T - t0 : TOK);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int NW = kRouteThreads / 32;
+
   const int vec_per_row = H / 8;
-  for (int i = threadIdx.x; i < kRouteTokens * vec_per_row; i += blockDim.x) {
+  for (int i = threadIdx.x; i < TOK * vec_per_row; i += blockDim.x) {
     const int t = i / vec_per_row, v = i - t * vec_per_row;
     uint4 val = make_uint4(0, 0, 0, 0);
-    if (t < nt) val = reinterpret_cast<const uint4*>(x + (t0 + t) * H)[v];
-    reinterpret_cast<uint4*>(xs + static_cast<int64_t>(t) * H)[v] = val;
+    if (t < nt) val = __ldg(reinterpret_cast<const uint4*>(x + (t0 + t) * H) + v);
+    const __nv_bfloat16* p = reinterpret_cast<const __nv_bfloat16*>(&val);
+    float4 lo, hi;
+    lo.x = __bfloat162float(p[0]); lo.y = __bfloat162float(p[1]);
+    lo.z = __bfloat162float(p[2]); lo.w = __bfloat162float(p[3]);
+    hi.x = __bfloat162float(p[4]); hi.y = __bfloat162float(p[5]);
+    hi.z = __bfloat162float(p[6]); hi.w = __bfloat162float(p[7]);
+    float4* dst = reinterpret_cast<float4*>(xs + static_cast<int64_t>(t) * H) + 2 * v;
+    dst[0] = lo;
+    dst[1] = hi;
   }
   __syncthreads();
 
-  // Each warp owns experts warp, warp + nwarps, ...; two experts at a time,
-  // with every 16-byte weight load of a lane issued before any is consumed, so
-  // that a warp waits for L2 about once per pair instead of once per vector.
-  const int nwarps = blockDim.x >> 5;
   constexpr int U = 8;  // vectors per lane per pass (H = 2048 -> one pass)
-  for (int e0 = warp; e0 < E; e0 += 2 * nwarps) {
-    const int e1 = e0 + nwarps;
-    float acc0[kRouteTokens], acc1[kRouteTokens];
+  for (int e0 = warp; e0 < E; e0 += 2 * NW) {
+    const int e1 = e0 + NW;
+    float acc0[TOK], acc1[TOK];
 #pragma unroll
-    for (int t = 0; t < kRouteTokens; ++t) acc0[t] = acc1[t] = 0.f;
+    for (int t = 0; t < TOK; ++t) acc0[t] = acc1[t] = 0.f;
     const uint4* w0 = reinterpret_cast<const uint4*>(gate_w + static_cast<int64_t>(e0) * H);
     const uint4* w1 = reinterpret_cast<const uint4*>(gate_w + static_cast<int64_t>(e1 < E ? e1 : e0) * H);
     for (int vb = 0; vb < vec_per_row; vb += 32 * U) {
@@ -134,21 +147,27 @@ __global__ void __launch_bounds__(512) route_kernel(const __nv_bfloat16* __restr
         if (v >= vec_per_row) break;
         const __nv_bfloat16* ap = reinterpret_cast<const __nv_bfloat16*>(&a[u]);
         const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(&b[u]);
+        float wa[8], wb[8];
 #pragma unroll
-        for (int t = 0; t < kRouteTokens; ++t) {
-          const uint4 xv = reinterpret_cast<const uint4*>(xs + static_cast<int64_t>(t) * H)[v];
-          const __nv_bfloat16* xp = reinterpret_cast<const __nv_bfloat16*>(&xv);
+        for (int i = 0; i < 8; ++i) {
+          wa[i] = __bfloat162float(ap[i]);
+          wb[i] = __bfloat162float(bp[i]);
+        }
+#pragma unroll
+        for (int t = 0; t < TOK; ++t) {
+          const float4* xv = reinterpret_cast<const float4*>(xs + static_cast<int64_t>(t) * H) + 2 * v;
+          const float4 x0 = xv[0], x1 = xv[1];
+          const float xf[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            const float xf = __bfloat162float(xp[i]);
-            acc0[t] = __fmaf_rn(xf, __bfloat162float(ap[i]), acc0[t]);
-            acc1[t] = __fmaf_rn(xf, __bfloat162float(bp[i]), acc1[t]);
+            acc0[t] = __fmaf_rn(xf[i], wa[i], acc0[t]);
+            acc1[t] = __fmaf_rn(xf[i], wb[i], acc1[t]);
           }
         }
       }
     }
 #pragma unroll
-    for (int t = 0; t < kRouteTokens; ++t) {
+    for (int t = 0; t < TOK; ++t) {
       const float l0 = round_bf16(warp_sum(acc0[t]));
       const float l1 = round_bf16(warp_sum(acc1[t]));
       if (lane == 0) {
@@ -159,6 +178,98 @@ __global__ void __launch_bounds__(512) route_kernel(const __nv_bfloat16* __restr
   }
   __syncthreads();
 
+  for (int tw = warp; tw < nt; tw += NW) {
+    const int64_t t = t0 + tw;
+    float v[kMaxExperts / 32];
+#pragma unroll
+    for (int j = 0; j < kMaxExperts / 32; ++j) {
+      const int id = lane + 32 * j;
+      float l = 0.f;
+      if (id < E) {
+        l = lg[tw * E + id];
+        if (logits_out != nullptr) logits_out[t * E + id] = __float2bfloat16_rn(l);
+        if (bias != nullptr) l = __fadd_rn(l, bias[id]);
+      }
+      v[j] = l;
+    }
+    warp_softmax_topk(v, E, k, renormalize, topk_w + t * k, topk_ids + t * k);
+  }
+}
+
+// Router on the tensor cores (mma.sync m16n8k16, bf16 in, fp32 accumulate):
+// 16 tokens x all E experts per block; the 16 warps split H into equal
+// slices, and the slices' partial logits are summed in warp order (a fixed
+// order, so the result is deterministic).  Within a 32-wide K chunk lane c of
+// a quad takes the contiguous elements 8c..8c+7 of both the token row and the
+// weight row, so every MMA pairs equal K indices.  Needs E % 8 == 0, E <= 64,
+// H % 512 == 0.
+constexpr int kRmWarps = 16;
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kRmWarps * 32) route_mma_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                  const __nv_bfloat16* __restrict__ gate_w,
+                                                                  int64_t T, int H, int k,
+                                                                  const float* __restrict__ bias, int renormalize,
+                                                                  __nv_bfloat16* __restrict__ logits_out,
+                                                                  float* __restrict__ topk_w,
+                                                                  int32_t* __restrict__ topk_ids) {
+  constexpr int E = NT * 8;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* part = reinterpret_cast<float*>(smem_raw);  // [warp][16 tokens][E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * 16;
+  const int slice = H / kRmWarps;
+  const int kbeg = warp * slice;
+  float acc[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+  const bool r0 = t0 + g < T, r1 = t0 + g + 8 < T;
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  const uint4* xa = reinterpret_cast<const uint4*>(x + (t0 + g) * H + kbeg) + c;
+  const uint4* xb = reinterpret_cast<const uint4*>(x + (t0 + g + 8) * H + kbeg) + c;
+  const uint4* wrow = reinterpret_cast<const uint4*>(gate_w + static_cast<int64_t>(g) * H + kbeg) + c;
+  const int64_t nstride = static_cast<int64_t>(8) * H / 8;  // uint4 per 8 weight rows
+#pragma unroll 2
+  for (int kc = 0; kc < slice; kc += 32) {
+    const int q = kc / 8;
+    const uint4 a_lo = r0 ? __ldg(xa + q) : zero;
+    const uint4 a_hi = r1 ? __ldg(xb + q) : zero;
+    uint4 b[NT];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) b[n] = __ldg(wrow + n * nstride + q);
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      mma_bf16_16816(acc[n], a_lo.x, a_hi.x, a_lo.y, a_hi.y, b[n].x, b[n].y);
+      mma_bf16_16816(acc[n], a_lo.z, a_hi.z, a_lo.w, a_hi.w, b[n].z, b[n].w);
+    }
+  }
+  float* pw = part + warp * 16 * E;
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    pw[g * E + n * 8 + 2 * c] = acc[n][0];
+    pw[g * E + n * 8 + 2 * c + 1] = acc[n][1];
+    pw[(g + 8) * E + n * 8 + 2 * c] = acc[n][2];
+    pw[(g + 8) * E + n * 8 + 2 * c + 1] = acc[n][3];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 16 * E; i += blockDim.x) {
+    float sum = 0.f;
+#pragma unroll
+    for (int w = 0; w < kRmWarps; ++w) sum = __fadd_rn(sum, part[w * 16 * E + i]);
+    part[i] = round_bf16(sum);  // warp 0's slice is read above before this write (same thread, same i)
+  }
+  __syncthreads();
+  const int nt = static_cast<int>(T - t0 < 16 ? T - t0 : 16);
   if (warp < nt) {
     const int64_t t = t0 + warp;
     float v[kMaxExperts / 32];
@@ -167,7 +278,7 @@ __global__ void __launch_bounds__(512) route_kernel(const __nv_bfloat16* __restr
       const int id = lane + 32 * j;
       float l = 0.f;
       if (id < E) {
-        l = lg[warp * E + id];
+        l = part[warp * E + id];
         if (logits_out != nullptr) logits_out[t * E + id] = __float2bfloat16_rn(l);
         if (bias != nullptr) l = __fadd_rn(l, bias[id]);
       }
@@ -509,25 +620,75 @@ inline unsigned grid_for(int64_t work, int threads) {
 
 }  // namespace
 
+template <int TOK>
+int launch_route(const void* x, const void* gate_w, int64_t T, int H, int E, int k, const float* bias,
+                 int renormalize, void* logits, float* topk_w, int32_t* topk_ids, cudaStream_t st) {
+  const size_t smem = static_cast<size_t>(TOK) * H * 4 + static_cast<size_t>(TOK) * E * 4;
+  if (smem > 200 * 1024) return fail(LLQ_EUNSUPPORTED, "hidden size %d too large for the router", H);
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(route_kernel<TOK>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr_set = true;
+  }
+  const unsigned blocks = static_cast<unsigned>((T + TOK - 1) / TOK);
+  route_kernel<TOK><<<blocks, kRouteThreads, smem, st>>>(static_cast<const __nv_bfloat16*>(x),
+                                                         static_cast<const __nv_bfloat16*>(gate_w), T, H, E, k,
+                                                         bias, renormalize, static_cast<__nv_bfloat16*>(logits),
+                                                         topk_w, topk_ids);
+  return check_launch("route_kernel");
+}
+
 int route_impl(const void* x, const void* gate_w, int64_t T, int H, int E, int k, const float* bias,
                int renormalize, void* logits, float* topk_w, int32_t* topk_ids, cudaStream_t st) {
   if (T <= 0) return LLQ_OK;
   if (E < 1 || E > kMaxExperts) return fail(LLQ_EUNSUPPORTED, "num_experts must be in [1, 256], got %d", E);
   if (k < 1 || k > E || k > 32) return fail(LLQ_EINVAL, "top_k must be in [1, min(E, 32)], got %d", k);
   if (H % 8 != 0) return fail(LLQ_EUNSUPPORTED, "hidden size must be a multiple of 8, got %d", H);
-  const size_t smem = static_cast<size_t>(kRouteTokens) * H * 2 + static_cast<size_t>(kRouteTokens) * E * 4;
-  if (smem > 200 * 1024) return fail(LLQ_EUNSUPPORTED, "hidden size %d too large for the router", H);
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr_set = true;
+  // enough blocks to cover the SMs at decode sizes, more tokens per weight pass at prefill sizes
+  static const int forced = [] {
+    const char* e = getenv("LLQ_ROUTE_TOK");
+    return e ? atoi(e) : 0;
+  }();
+  if (forced == 0 && E % 8 == 0 && E <= 64 && H % (kRmWarps * 32) == 0) {
+    const size_t smem = static_cast<size_t>(kRmWarps) * 16 * E * 4;
+    const unsigned blocks = static_cast<unsigned>((T + 15) / 16);
+    auto* xp = static_cast<const __nv_bfloat16*>(x);
+    auto* wp = static_cast<const __nv_bfloat16*>(gate_w);
+    auto* lp = static_cast<__nv_bfloat16*>(logits);
+#define LLQ_ROUTE_MMA(NT)                                                                                  \
+  case NT: {                                                                                               \
+    static bool attr = false;                                                                              \
+    if (!attr) {                                                                                           \
+      cudaFuncSetAttribute(route_mma_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);  \
+      attr = true;                                                                                         \
+    }                                                                                                      \
+    route_mma_kernel<NT><<<blocks, kRmWarps * 32, smem, st>>>(xp, wp, T, H, k, bias, renormalize, lp, topk_w, \
+                                                              topk_ids);                                   \
+    return check_launch("route_mma_kernel");                                                               \
   }
-  const unsigned blocks = static_cast<unsigned>((T + kRouteTokens - 1) / kRouteTokens);
-  route_kernel<<<blocks, 512, smem, st>>>(static_cast<const __nv_bfloat16*>(x),
-                                          static_cast<const __nv_bfloat16*>(gate_w), T, H, E, k,
-                                          bias, renormalize, static_cast<__nv_bfloat16*>(logits),
-                                          topk_w, topk_ids);
-  return check_launch("route_kernel");
+    switch (E / 8) {
+      LLQ_ROUTE_MMA(1)
+      LLQ_ROUTE_MMA(2)
+      LLQ_ROUTE_MMA(3)
+      LLQ_ROUTE_MMA(4)
+      LLQ_ROUTE_MMA(5)
+      LLQ_ROUTE_MMA(6)
+      LLQ_ROUTE_MMA(7)
+      LLQ_ROUTE_MMA(8)
+      default: break;
+    }
+#undef LLQ_ROUTE_MMA
+  }
+  const int sms = num_sms();
+  int tok = T <= sms ? 1 : T <= 2 * sms ? 2 : T <= 8 * sms ? 4 : 8;
+  if (forced == 1 || forced == 2 || forced == 4 || forced == 8) tok = forced;
+  if (static_cast<size_t>(tok) * H * 4 + static_cast<size_t>(tok) * E * 4 > 200 * 1024) tok = 1;
+  switch (tok) {
+    case 1: return launch_route<1>(x, gate_w, T, H, E, k, bias, renormalize, logits, topk_w, topk_ids, st);
+    case 2: return launch_route<2>(x, gate_w, T, H, E, k, bias, renormalize, logits, topk_w, topk_ids, st);
+    case 4: return launch_route<4>(x, gate_w, T, H, E, k, bias, renormalize, logits, topk_w, topk_ids, st);
+    default: return launch_route<8>(x, gate_w, T, H, E, k, bias, renormalize, logits, topk_w, topk_ids, st);
+  }
 }
 
 int route_topk_impl(const void* logits, int dtype, int64_t T, int E, int k, const float* bias,
