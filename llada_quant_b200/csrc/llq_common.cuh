@@ -7,6 +7,8 @@
 #include <stdint.h>
 #include <stdio.h>
 #include <string>
+#include <cstdlib>
+#include <utility>
 
 #include "../../include/llada_quant.h"
 
@@ -35,6 +37,40 @@ inline int num_sms() {
     if (n <= 0) n = 148;
   }
   return n;
+}
+
+// ---------------------------------------------------------------------------
+// programmatic dependent launch: the layer's kernels are launched so that the
+// next one is scheduled while the previous one drains; each waits for its
+// predecessor's results (griddepcontrol.wait, a no-op without the attribute)
+// before reading them and releases its dependents once its work is issued.
+// LLQ_PDL=0 turns the attribute off.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("LLQ_PDL");
+    return e == nullptr || atoi(e) != 0;
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // device error word (bounded waits record where they gave up)

@@ -45,7 +45,6 @@ namespace {
 
 constexpr int KC = 128;
 constexpr int ROWS = 128;
-constexpr int EPI_WARPS = 8;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int MAX_G = 16;  // scale groups per row (K <= 2048 at group 128)
 constexpr int MAX_E = 256;
@@ -86,12 +85,20 @@ struct Cfg {
   // then ALU-bound -- so SPLIT stays 1; the code keeps both layouts correct)
   static constexpr int SPLIT = 1;
   static constexpr int MMA_WARPS = 2 * SPLIT;
+  // (measured at C3: 16 dequantizing warps with one epilogue warpgroup made
+  // the exact GEMM1 11% slower than 8 + 8; the code supports both)
   static constexpr int DQ_WARPS = 8;
+  static constexpr int EPI_WARPS = 8;  // token groups of one warpgroup each
   static constexpr int DQ_PARTS = DQ_WARPS / 8;  // warpgroups per weight tile
   static constexpr int FIRST_DQ = 1 + MMA_WARPS;
   static constexpr int FIRST_EPI = FIRST_DQ + DQ_WARPS;
   static constexpr int THREADS = (FIRST_EPI + EPI_WARPS) * 32;
-  static constexpr int ACC_COLS = FAST ? 4 * NTM : 2 * SPLIT * NTM;
+  // exact mode: the accumulators are double-buffered across items when they
+  // fit beside two A stages, so that an item's epilogue overlaps the next
+  // item's MMAs (64-token tiles); 128-token tiles keep one buffer
+  static constexpr int ACC_BUFS = (!FAST && 2 * 2 * SPLIT * NTM <= 256) ? 2 : 1;
+  static constexpr int ACC_BUF_COLS = 2 * SPLIT * NTM;
+  static constexpr int ACC_COLS = FAST ? 4 * NTM : ACC_BUFS * ACC_BUF_COLS;
   static constexpr int A_STAGE_COLS = KC;  // 64 columns per tile
   static constexpr int A_STAGES_FIT = static_cast<int>(TMEM_COLS - ACC_COLS) / A_STAGE_COLS;
   static constexpr int A_STAGES = A_STAGES_FIT > 4 ? 4 : A_STAGES_FIT;
@@ -386,7 +393,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
   uint64_t* a_full = mdone + S;         // [2 tiles][AS]: TMEM A stage written
   uint64_t* sc_full = a_full + 2 * AS;  // [2]
   uint64_t* sc_empty = sc_full + 2;     // [2]
-  uint64_t* acc_full = sc_empty + 2;    // [2] (exact uses [0])
+  uint64_t* acc_full = sc_empty + 2;    // [2] (per item in exact mode, per step in fast mode)
   uint64_t* acc_empty = acc_full + 2;   // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -395,6 +402,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = args.E;
   const int G = args.groups;
+  pdl_wait();
   const int kch = args.K / KC;
 
   // ---- compacted work list: token tiles per expert, prefix-summed by warp 0
@@ -436,9 +444,9 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     for (int i = 0; i < 2 * AS; ++i) mbar_init(&a_full[i], DQ_WARPS / 2);  // per tile
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sc_full[i], 1);
-      mbar_init(&sc_empty[i], FAST ? DQ_WARPS + EPI_WARPS : DQ_WARPS);
+      mbar_init(&sc_empty[i], FAST ? DQ_WARPS + C::EPI_WARPS : DQ_WARPS);
       mbar_init(&acc_full[i], MMA_WARPS);
-      mbar_init(&acc_empty[i], EPI_WARPS);
+      mbar_init(&acc_empty[i], C::EPI_WARPS);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -537,12 +545,15 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         const int box = 16 << box_index(item.rows_t);
         const uint32_t idesc = make_idesc(nt);
         if (!FAST) {
-          if (!mbar_wait_sleep(&acc_empty[0], (ii & 1) ^ 1, abort_flag, 0x200)) break;
+          const int ab = C::ACC_BUFS == 2 ? (ii & 1) : 0;
+          const uint32_t ph = C::ACC_BUFS == 2 ? ((ii >> 1) & 1) : (ii & 1);
+          if (!mbar_wait_sleep(&acc_empty[ab], ph ^ 1, abort_flag, 0x200)) break;
           tc_fence_after();
         }
         for (int kc = 0; kc < kch; ++kc, ++it) {
           const int s = it % S, sa = it % AS;
-          uint32_t d0 = tmem + par * NTM, d1 = tmem + (SPLIT + par) * NTM;
+          const uint32_t acc_base = tmem + (C::ACC_BUFS == 2 ? (ii & 1) * C::ACC_BUF_COLS : 0);
+          uint32_t d0 = acc_base + par * NTM, d1 = acc_base + (SPLIT + par) * NTM;
           if (FAST) {
             const int pb = it & 1;
             if (!mbar_wait(&acc_empty[pb], ((it >> 1) & 1) ^ 1, abort_flag, 0x210 + pb)) { ok = false; break; }
@@ -566,10 +577,13 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
             const uint64_t bdesc = bdesc0 + (j >> 2) * half_step + (j & 3) * 2;
             const uint32_t acc = jj > 0 ? 1u : first;
             if (!(args.debug & 2)) tc_mma(d, a_stage + j * 8, bdesc, idesc, acc);
+#ifdef LLQ_TRACE
+            if (tile == 0 && it >= 16 && it < 24) LLQ_TRACE_AT(7, (it - 16) * 8 + jj);
+#endif
           }
           tc_commit(&mdone[s]);
           if (tile == 0) LLQ_TRACE_AT(6, it);
-          if (!FAST && kc == kch - 1) tc_commit(&acc_full[0]);
+          if (!FAST && kc == kch - 1) tc_commit(&acc_full[C::ACC_BUFS == 2 ? (ii & 1) : 0]);
         }
       }
     }
@@ -652,13 +666,14 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     const int q = warp & 3;
     const int r = q * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
-    constexpr int HALF = NTM / 2;
+    constexpr int EG = C::EPI_WARPS / 4;  // token groups, one epilogue warpgroup each
+    constexpr int HALF = NTM / EG;
     int it = 0;
     bool ok = true;
     for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
       const Item item = item_at(u);
       const int nt = (item.rows_t + 15) & ~15;
-      const int t_begin = eg * (nt / 2), t_end = (eg + 1) * (nt / 2);
+      const int t_begin = eg * (nt / EG), t_end = (eg + 1) * (nt / EG);
       // one token's outputs from the two fp32 accumulators of row r
       auto emit = [&](int t, float a0, float a1) {
         if (t >= t_end || t >= item.rows_t) return;
@@ -725,19 +740,22 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
 #pragma unroll
         for (int i = 0; i < (FAST ? HALF : 1); ++i) emit(t_begin + i, acc0[i], acc1[i]);
       } else {
-        if (!mbar_wait_sleep(&acc_full[0], ii & 1, abort_flag, 0x420)) break;
+        const int ab = C::ACC_BUFS == 2 ? (ii & 1) : 0;
+        const uint32_t ph = C::ACC_BUFS == 2 ? ((ii >> 1) & 1) : (ii & 1);
+        const uint32_t acc_base = tmem + ab * C::ACC_BUF_COLS;
+        if (!mbar_wait_sleep(&acc_full[ab], ph, abort_flag, 0x420)) break;
         tc_fence_after();
 #pragma unroll
         for (int c = 0; c < HALF / 8; ++c) {
           const int t0 = t_begin + c * 8;
           if (t0 < t_end) {
             float v0[8], v1[8];
-            tc_ld8(tmem + lane_addr + t0, v0);
-            tc_ld8(tmem + lane_addr + SPLIT * NTM + t0, v1);
+            tc_ld8(acc_base + lane_addr + t0, v0);
+            tc_ld8(acc_base + lane_addr + SPLIT * NTM + t0, v1);
             if (SPLIT == 2) {
               float w0[8], w1[8];
-              tc_ld8(tmem + lane_addr + NTM + t0, w0);
-              tc_ld8(tmem + lane_addr + 3 * NTM + t0, w1);
+              tc_ld8(acc_base + lane_addr + NTM + t0, w0);
+              tc_ld8(acc_base + lane_addr + 3 * NTM + t0, w1);
 #pragma unroll
               for (int i = 0; i < 8; ++i) {
                 v0[i] = __fadd_rn(v0[i], w0[i]);
@@ -750,7 +768,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[0]);
+        if (lane == 0) mbar_arrive(&acc_empty[ab]);
       }
     }
   }
@@ -758,6 +776,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
   if (!GEMM1 && args.ep_on && warp >= FIRST_EPI) __threadfence_system();  // rows stored to peers
   tc_fence_before();
   __syncthreads();
+  pdl_trigger();
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
@@ -852,8 +871,8 @@ int launch_tc(const void* act, int64_t n_rows, const int32_t* offsets, int E, in
     attr = true;
   }
   const int grid = num_sms();
-  moe_gemm_tc_kernel<GEMM1, BITS, FAST, NTM><<<grid, C::THREADS, C::SMEM_BYTES, st>>>(tw, tb[0], tb[1], tb[2],
-                                                                                  tb[3], a);
+  launch_pdl(moe_gemm_tc_kernel<GEMM1, BITS, FAST, NTM>, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, st, tw, tb[0],
+             tb[1], tb[2], tb[3], a);
   return check_launch("moe_gemm_tc_kernel");
 }
 

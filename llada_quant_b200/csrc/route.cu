@@ -225,6 +225,7 @@ __global__ void __launch_bounds__(kRmWarps * 32) route_mma_kernel(const __nv_bfl
   constexpr int E = NT * 8;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* part = reinterpret_cast<float*>(smem_raw);  // [warp][16 tokens][E]
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * 16;
@@ -269,6 +270,7 @@ __global__ void __launch_bounds__(kRmWarps * 32) route_mma_kernel(const __nv_bfl
     part[i] = round_bf16(sum);  // warp 0's slice is read above before this write (same thread, same i)
   }
   __syncthreads();
+  pdl_trigger();
   const int nt = static_cast<int>(T - t0 < 16 ? T - t0 : 16);
   if (warp < nt) {
     const int64_t t = t0 + warp;
@@ -435,6 +437,7 @@ __global__ void __launch_bounds__(kAlignSmallThreads) align_small_kernel(
   __shared__ int32_t cursor[kMaxExperts];
   __shared__ int32_t wcnt[W][kMaxExperts];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  pdl_wait();
   for (int i = tid; i < kMaxExperts; i += blockDim.x) cnt[i] = 0;
   for (int i = tid; i < W * kMaxExperts; i += blockDim.x) (&wcnt[0][0])[i] = 0;
   if (m.counts != nullptr) {
@@ -513,6 +516,7 @@ __global__ void permute_kernel(const uint4* __restrict__ x, int64_t n_rows, int 
                                const int32_t* __restrict__ sorted_slots, uint4* __restrict__ xs,
                                const int32_t* __restrict__ n_dev) {
   // n_dev (optional): the number of sorted rows, known only on the device
+  pdl_wait();
   const int64_t total = (n_dev != nullptr ? static_cast<int64_t>(*n_dev) : n_rows) * vec_per_row;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -533,6 +537,7 @@ __global__ void permute_kernel(const uint4* __restrict__ x, int64_t n_rows, int 
 
 __global__ void combine_kernel(const uint4* __restrict__ y, int64_t T, int k, int vec_per_row,
                                uint4* __restrict__ out) {
+  pdl_wait();
   const int64_t total = T * vec_per_row;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -662,8 +667,8 @@ int route_impl(const void* x, const void* gate_w, int64_t T, int H, int E, int k
       cudaFuncSetAttribute(route_mma_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);  \
       attr = true;                                                                                         \
     }                                                                                                      \
-    route_mma_kernel<NT><<<blocks, kRmWarps * 32, smem, st>>>(xp, wp, T, H, k, bias, renormalize, lp, topk_w, \
-                                                              topk_ids);                                   \
+    launch_pdl(route_mma_kernel<NT>, dim3(blocks), dim3(kRmWarps * 32), smem, st, xp, wp, T, H, k, bias,    \
+               renormalize, lp, topk_w, topk_ids);                                                         \
     return check_launch("route_mma_kernel");                                                               \
   }
     switch (E / 8) {
@@ -725,7 +730,8 @@ int align_impl_masked(const int32_t* ids, int64_t n, int E, int32_t* offsets, in
     return check_launch("align memset");
   }
   if (n <= kAlignSmallMax) {
-    align_small_kernel<<<1, kAlignSmallThreads, 0, st>>>(ids, static_cast<int>(n), E, offsets, sorted_slots, m);
+    launch_pdl(align_small_kernel, dim3(1), dim3(kAlignSmallThreads), 0, st, ids, static_cast<int>(n), E, offsets,
+               sorted_slots, m);
     return check_launch("align_small_kernel");
   }
   const int64_t nblk = (n + kAlignChunk - 1) / kAlignChunk;
@@ -759,11 +765,11 @@ int permute_impl(const void* x, int64_t T, int H, int k, const int32_t* sorted_s
   if (n == 0) return LLQ_OK;
   const int vpr = H / 8;
   if (kperm)
-    permute_kernel<true><<<grid_for(n * vpr, 256), 256, 0, st>>>(static_cast<const uint4*>(x), n, vpr, k,
-                                                                 sorted_slots, static_cast<uint4*>(xs), n_dev);
+    launch_pdl(permute_kernel<true>, dim3(grid_for(n * vpr, 256)), dim3(256), 0, st, static_cast<const uint4*>(x), n,
+               vpr, k, sorted_slots, static_cast<uint4*>(xs), n_dev);
   else
-    permute_kernel<false><<<grid_for(n * vpr, 256), 256, 0, st>>>(static_cast<const uint4*>(x), n, vpr, k,
-                                                                  sorted_slots, static_cast<uint4*>(xs), n_dev);
+    launch_pdl(permute_kernel<false>, dim3(grid_for(n * vpr, 256)), dim3(256), 0, st, static_cast<const uint4*>(x),
+               n, vpr, k, sorted_slots, static_cast<uint4*>(xs), n_dev);
   return check_launch("permute_kernel");
 }
 
@@ -794,8 +800,8 @@ int combine_impl(const void* y, int64_t T, int k, int H, void* out, cudaStream_t
   if (H % 8 != 0) return fail(LLQ_EUNSUPPORTED, "hidden size must be a multiple of 8");
   if (T == 0) return LLQ_OK;
   const int vpr = H / 8;
-  combine_kernel<<<grid_for(T * vpr, 256), 256, 0, st>>>(static_cast<const uint4*>(y), T, k, vpr,
-                                                         static_cast<uint4*>(out));
+  launch_pdl(combine_kernel, dim3(grid_for(T * vpr, 256)), dim3(256), 0, st, static_cast<const uint4*>(y), T, k, vpr,
+             static_cast<uint4*>(out));
   return check_launch("combine_kernel");
 }
 
