@@ -229,6 +229,18 @@ int llq_moe_gemm2(const void* h_sorted, const int32_t* expert_offsets,
                   int H, int I, const int8_t* qw2, const float* sw2, int bits, int group_size,
                   void* y_slots, int impl, void* stream);
 
+/*
+ * Dense QuantLinear forward on the same kernel (replaces runtime/linear.py:127-131,
+ * F.linear(x, dequantize_weight()) without the bias add): out[m, n] =
+ * bf16(sum_k x[m, k] * bf16(q[n, k] * s[n, k / group])), fp32 accumulation.
+ * x bf16 [M, K], qweight int8 [N, K/2 or K], scale fp32 [N, K/group], out bf16 [M, N].
+ * Exact weights only (LLQ_GEMM_AUTO or LLQ_GEMM_TCGEN05); K % 128 == 0, K <= 2048,
+ * N % 256 == 0, group % 128 == 0 (others return LLQ_EUNSUPPORTED).
+ */
+int llq_quant_linear(const void* x, int64_t M, int K, int N, const int8_t* qweight,
+                     const float* scale, int bits, int group_size, void* out, int impl,
+                     void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Whole layer.                                                              */
 /* ------------------------------------------------------------------------ */

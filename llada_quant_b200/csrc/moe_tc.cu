@@ -125,6 +125,7 @@ struct TcArgs {
   int groups;      // scales per row
   int debug;       // development switch: 1 = no dequant math, 2 = no MMA, 4 = no TMEM stores,
                    // 8 = no token-tile loads (results are wrong)
+  int dense_rows;  // offsets == nullptr: one expert of this many rows, identity slots, weight 1
   int ep_on;       // GEMM2 only: scatter rows into the peers' back regions and signal them
   EpScatter ep;
 };
@@ -414,7 +415,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
       const int e = lane * (MAX_E / 32) + j;
       int n = 0;
       if (e < E) {
-        const int m = args.offsets[e + 1] - args.offsets[e];
+        const int m = args.offsets != nullptr ? args.offsets[e + 1] - args.offsets[e] : args.dense_rows;
         n = (m + NTM - 1) / NTM;
       }
       local[j] = n;
@@ -476,8 +477,8 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     }
     it.e = lo;
     it.tt = tg - tile_prefix[lo];
-    const int base = args.offsets[lo];
-    const int m = args.offsets[lo + 1] - base;
+    const int base = args.offsets != nullptr ? args.offsets[lo] : 0;
+    const int m = args.offsets != nullptr ? args.offsets[lo + 1] - base : args.dense_rows;
     it.row0 = base + it.tt * NTM;
     it.rows_t = min(NTM, m - it.tt * NTM);
     return it;
@@ -686,8 +687,8 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           const int pos = FAST ? kperm_pos(n) : n;
           args.out[p * args.n_out + pos] = __float2bfloat16_rn(__fmul_rn(silu, up));
         } else {
-          const int32_t slot = args.sorted_slots[p];
-          const float w = args.topk_w[slot];
+          const int32_t slot = args.sorted_slots != nullptr ? args.sorted_slots[p] : static_cast<int32_t>(p);
+          const float w = args.topk_w != nullptr ? args.topk_w[slot] : 1.f;
           __nv_bfloat16* orow;
           if (args.ep_on) {
             const int src = slot / args.ep.L.cap;
@@ -844,6 +845,7 @@ int launch_tc(const void* act, int64_t n_rows, const int32_t* offsets, int E, in
   }
   TcArgs a;
   a.offsets = offsets;
+  a.dense_rows = offsets == nullptr ? static_cast<int>(n_rows) : 0;
   a.scale = scale;
   a.sorted_slots = sorted_slots;
   a.topk_w = topk_w;

@@ -74,10 +74,18 @@ def fused_moe(hidden_states: torch.Tensor, w1, w2, gating_output: Optional[torch
 
 def moe_layer(x: torch.Tensor, gate_w: torch.Tensor, packed: PackedExperts, top_k: int,
               bias: Optional[torch.Tensor] = None, renormalize: bool = False,
-              impl: str = "auto") -> torch.Tensor:
+              impl: str = "auto", recorder=None) -> torch.Tensor:
     """Router + routed experts, the forward of a PACKED LLaDA MoE block: one router
-    kernel (bf16 logits, fp32 softmax, top-k) then :func:`fused_moe`."""
+    kernel (bf16 logits, fp32 softmax, top-k) then :func:`fused_moe`.  With a
+    ``routing_stats.RoutingRecorder`` the call's per-expert loads are added to it on
+    the device, from the expert offsets the GEMMs used."""
     # eager hot path: the op implementations directly (no per-call dispatcher cost)
     topk_w, topk_ids, _ = ops._route_impl(x, gate_w, top_k, bias, renormalize)
-    return ops._fused_moe_packed_impl(x, packed.qw1, packed.sw1, packed.qw2, packed.sw2, topk_w,
-                                      topk_ids, packed.bits, IMPL[impl])
+    out = ops._fused_moe_packed_impl(x, packed.qw1, packed.sw1, packed.qw2, packed.sw2, topk_w,
+                                     topk_ids, packed.bits, IMPL[impl])
+    if recorder is not None:
+        E = packed.num_experts
+        T = x.shape[0]
+        ws = ops.moe_workspace(T, top_k, E, packed.hidden, packed.intermediate, x.device)
+        recorder.record_offsets(ws[:4 * (E + 1)].view(torch.int32), T, top_k)  # offsets lead the workspace
+    return out

@@ -403,6 +403,27 @@ def moe_workspace(T: int, k: int, E: int, H: int, I: int, device) -> torch.Tenso
     return ws
 
 
+def _quant_linear_impl(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor, bits: int) -> torch.Tensor:
+    """``F.linear(x, dequantize(qweight, scale))`` on the tcgen05 kernel: x bf16 [M, K] -> bf16 [M, N]."""
+    _need_cuda(x, qweight, scale)
+    x = x.contiguous()
+    M, K = x.shape
+    N = qweight.shape[0]
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+    check(load().llq_quant_linear(x.data_ptr(), M, K, N, qweight.data_ptr(), scale.data_ptr(), bits,
+                                  _group_of(qweight, scale, bits), out.data_ptr(), 0, _stream(x)),
+          "quant_linear")
+    return out
+
+
+quant_linear = torch.library.custom_op("llada_quant::quant_linear", mutates_args=())(_quant_linear_impl)
+
+
+@quant_linear.register_fake
+def _(x, qweight, scale, bits):
+    return x.new_empty(x.shape[0], qweight.shape[0], dtype=torch.bfloat16)
+
+
 def _fused_moe_packed_impl(x: torch.Tensor, qw1: torch.Tensor, sw1: torch.Tensor, qw2: torch.Tensor,
                      sw2: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor, bits: int,
                      impl: int) -> torch.Tensor:
