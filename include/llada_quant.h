@@ -235,11 +235,15 @@ int llq_moe_gemm2(const void* h_sorted, const int32_t* expert_offsets,
  * bf16(sum_k x[m, k] * bf16(q[n, k] * s[n, k / group])), fp32 accumulation.
  * x bf16 [M, K], qweight int8 [N, K/2 or K], scale fp32 [N, K/group], out bf16 [M, N].
  * Exact weights only (LLQ_GEMM_AUTO or LLQ_GEMM_TCGEN05); K % 128 == 0, K <= 2048,
- * N % 256 == 0, group % 128 == 0 (others return LLQ_EUNSUPPORTED).
+ * N % 256 == 0, group % 128 == 0 (others return LLQ_EUNSUPPORTED).  When the layer
+ * has fewer output tiles than SMs, K is split into slices whose fp32 partial sums
+ * go to the workspace (llq_quant_linear_workspace_size bytes, 0 when unsplit) and
+ * are added in slice order by a second kernel.
  */
+size_t llq_quant_linear_workspace_size(int64_t M, int K, int N);
 int llq_quant_linear(const void* x, int64_t M, int K, int N, const int8_t* qweight,
-                     const float* scale, int bits, int group_size, void* out, int impl,
-                     void* stream);
+                     const float* scale, int bits, int group_size, void* out, void* workspace,
+                     size_t workspace_bytes, int impl, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Whole layer.                                                              */

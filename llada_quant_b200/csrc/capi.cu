@@ -30,6 +30,8 @@ int fail(int code, const char* fmt, ...) {
 
 const char* last_error() { return t_error; }
 
+constexpr int KC_STEP = 128;
+
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct MoeWorkspace {
@@ -174,8 +176,14 @@ int llq_moe_gemm2(const void* h_sorted, const int32_t* expert_offsets, const int
                     group_size, y_slots, as_stream(stream));
 }
 
+size_t llq_quant_linear_workspace_size(int64_t M, int K, int N) {
+  if (M <= 0 || K < KC_STEP || N < 1) return 0;
+  const int ks = dense_ksplit(M, K, N);
+  return ks > 1 ? static_cast<size_t>(ks) * M * N * 4 : 0;
+}
+
 int llq_quant_linear(const void* x, int64_t M, int K, int N, const int8_t* qweight, const float* scale, int bits,
-                     int group_size, void* out, int impl, void* stream) {
+                     int group_size, void* out, void* workspace, size_t workspace_bytes, int impl, void* stream) {
   if (M < 0 || K < 1 || N < 1) return fail(LLQ_EINVAL, "bad shape M=%lld K=%d N=%d", (long long)M, K, N);
   if (bits != 4 && bits != 8) return fail(LLQ_EUNSUPPORTED, "bits must be 8 or 4, got %d", bits);
   if (bits == 4 && K % 2 != 0) return fail(LLQ_EINVAL, "int4 packing needs an even last dimension");
@@ -183,11 +191,8 @@ int llq_quant_linear(const void* x, int64_t M, int K, int N, const int8_t* qweig
   if (impl != LLQ_GEMM_AUTO && impl != LLQ_GEMM_TCGEN05)
     return fail(LLQ_EUNSUPPORTED, "the dense W%dA16 linear runs the exact tcgen05 kernel only", bits);
   if (M > 0x7fffffff) return fail(LLQ_EINVAL, "too many rows");
-  if (!tc_supported(1, N, K, bits, group_size, false))
-    return fail(LLQ_EUNSUPPORTED, "tcgen05 dense linear needs K %% 128 == 0, K <= 2048, N %% 256 == 0 and "
-                                  "group %% 128 == 0 (K=%d N=%d group=%d)", K, N, group_size);
-  return gemm2_tc(x, nullptr, nullptr, nullptr, M, 1, N, K, qweight, scale, bits, group_size, out, false,
-                  as_stream(stream), M, nullptr);
+  return dense_linear_tc(x, M, K, N, qweight, scale, bits, group_size, out, workspace, workspace_bytes,
+                         as_stream(stream));
 }
 
 size_t llq_moe_workspace_size(int64_t T, int k, int E, int H, int I) {

@@ -34,6 +34,9 @@ int gemm2_tc(const void*, const int32_t*, const int32_t*, const float*, int64_t,
              const EpScatter* ep = nullptr);
 bool tc_supported(int E, int N_out, int K, int bits, int group_size, bool gemm1);
 
+int dense_ksplit(int64_t M, int K, int N);
+int dense_linear_tc(const void* x, int64_t M, int K, int N, const int8_t* q, const float* scale, int bits,
+                    int group_size, void* out, void* workspace, size_t ws_bytes, cudaStream_t st);
 int align_impl_masked(const int32_t*, int64_t, int, int32_t*, int32_t*, void*, size_t, cudaStream_t,
                       const AlignMask&);
 

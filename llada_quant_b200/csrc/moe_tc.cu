@@ -126,6 +126,8 @@ struct TcArgs {
   int debug;       // development switch: 1 = no dequant math, 2 = no MMA, 4 = no TMEM stores,
                    // 8 = no token-tile loads (results are wrong)
   int dense_rows;  // offsets == nullptr: one expert of this many rows, identity slots, weight 1
+  int ksplit;      // K slices per output tile (> 1: exact GEMM2 only, fp32 partials to `partial`)
+  float* partial;  // [ksplit][rows][n_out] when ksplit > 1
   int ep_on;       // GEMM2 only: scatter rows into the peers' back regions and signal them
   EpScatter ep;
 };
@@ -363,7 +365,7 @@ __device__ __forceinline__ int box_index(int rows) {
 }
 
 struct Item {
-  int e, tt, rb, row0, rows_t;
+  int e, tt, rb, row0, rows_t, ks;
 };
 
 // ---------------------------------------------------------------------------
@@ -464,12 +466,15 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int total_tiles = tile_prefix[E];
-  const int total_items = total_tiles * args.rblocks;
+  const int total_items = total_tiles * args.rblocks * args.ksplit;
+  const int kper = kch / args.ksplit;  // K steps per item
 
   auto item_at = [&](int u) -> Item {
     Item it;
-    const int tg = u / args.rblocks;
-    it.rb = u - tg * args.rblocks;
+    const int uu = u / args.ksplit;
+    it.ks = u - uu * args.ksplit;
+    const int tg = uu / args.rblocks;
+    it.rb = uu - tg * args.rblocks;
     int lo = 0, hi = E;  // largest e with tile_prefix[e] <= tg
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
@@ -508,7 +513,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         const int box = 16 << bi;
         const CUtensorMap* tb = bi == 0 ? &tm_b0 : bi == 1 ? &tm_b1 : bi == 2 ? &tm_b2 : &tm_b3;
         const int w0 = static_cast<int>(wrow_of(item, 0)), w1 = static_cast<int>(wrow_of(item, 1));
-        for (int kc = 0; kc < kch; ++kc, ++it) {
+        for (int kc = item.ks * kper; kc < (item.ks + 1) * kper; ++kc, ++it) {
           const int s = it % S;
           if (!mbar_wait_sleep(&wfree[s], ((it / S) & 1) ^ 1, abort_flag, 0x110 + s)) { ok = false; break; }
           if (!mbar_wait_sleep(&mdone[s], ((it / S) & 1) ^ 1, abort_flag, 0x118 + s)) { ok = false; break; }
@@ -551,7 +556,8 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           if (!mbar_wait_sleep(&acc_empty[ab], ph ^ 1, abort_flag, 0x200)) break;
           tc_fence_after();
         }
-        for (int kc = 0; kc < kch; ++kc, ++it) {
+        const int kbeg = item.ks * kper, kend = kbeg + kper;
+        for (int kc = kbeg; kc < kend; ++kc, ++it) {
           const int s = it % S, sa = it % AS;
           const uint32_t acc_base = tmem + (C::ACC_BUFS == 2 ? (ii & 1) * C::ACC_BUF_COLS : 0);
           uint32_t d0 = acc_base + par * NTM, d1 = acc_base + (SPLIT + par) * NTM;
@@ -571,7 +577,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           const uint64_t half_step = static_cast<uint64_t>((box * 128) >> 4);
           const uint32_t a_stage = a_base + sa * C::A_STAGE_COLS + tile * (KC / 2);
           const uint32_t d = tile ? d1 : d0;
-          const uint32_t first = FAST ? 0u : (kc > 0 ? 1u : 0u);
+          const uint32_t first = FAST ? 0u : (kc > kbeg ? 1u : 0u);
 #pragma unroll
           for (int jj = 0; jj < KC / 16 / SPLIT; ++jj) {
             const int j = jj * SPLIT + par;
@@ -584,7 +590,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           }
           tc_commit(&mdone[s]);
           if (tile == 0) LLQ_TRACE_AT(6, it);
-          if (!FAST && kc == kch - 1) tc_commit(&acc_full[C::ACC_BUFS == 2 ? (ii & 1) : 0]);
+          if (!FAST && kc == kend - 1) tc_commit(&acc_full[C::ACC_BUFS == 2 ? (ii & 1) : 0]);
         }
       }
     }
@@ -603,7 +609,8 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
       const int sbuf = ii & 1;
       if (!mbar_wait(&sc_full[sbuf], (ii >> 1) & 1, abort_flag, 0x300)) break;
       const float* srow = ssc + sbuf * (2 * ROWS * MAX_G) + wg * (ROWS * MAX_G) + r * G;
-      for (int kc = 0; kc < kch; ++kc, ++it) {
+      const int kbeg = (u % args.ksplit) * kper;
+      for (int kc = kbeg; kc < kbeg + kper; ++kc, ++it) {
         const int s = it % S, sa = it % AS;
         if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, 0x310 + s)) { ok = false; break; }
         if (warp == FIRST_DQ) LLQ_TRACE_AT(1, it);
@@ -687,6 +694,13 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           const int pos = FAST ? kperm_pos(n) : n;
           args.out[p * args.n_out + pos] = __float2bfloat16_rn(__fmul_rn(silu, up));
         } else {
+          if (args.ksplit > 1) {  // fp32 partial of this K slice, summed in order by splitk_reduce
+            float* prow = args.partial + (static_cast<int64_t>(item.ks) * args.dense_rows + p) * args.n_out +
+                          item.rb * 2 * ROWS + r;
+            prow[0] = a0;
+            prow[ROWS] = a1;
+            return;
+          }
           const int32_t slot = args.sorted_slots != nullptr ? args.sorted_slots[p] : static_cast<int32_t>(p);
           const float w = args.topk_w != nullptr ? args.topk_w[slot] : 1.f;
           __nv_bfloat16* orow;
@@ -828,7 +842,7 @@ template <bool GEMM1, int BITS, bool FAST, int NTM>
 int launch_tc(const void* act, int64_t n_rows, const int32_t* offsets, int E, int K, int rows_total,
               int inter, int n_out, const int8_t* q, const float* scale, int group_size,
               const int32_t* sorted_slots, const float* topk_w, void* out, cudaStream_t st,
-              const EpScatter* ep) {
+              const EpScatter* ep, int ksplit = 1, float* partial = nullptr) {
   using C = Cfg<GEMM1, BITS, FAST, NTM>;
   if (n_rows <= 0) return LLQ_OK;
   CUtensorMap tw, tb[4];
@@ -846,6 +860,8 @@ int launch_tc(const void* act, int64_t n_rows, const int32_t* offsets, int E, in
   TcArgs a;
   a.offsets = offsets;
   a.dense_rows = offsets == nullptr ? static_cast<int>(n_rows) : 0;
+  a.ksplit = ksplit;
+  a.partial = partial;
   a.scale = scale;
   a.sorted_slots = sorted_slots;
   a.topk_w = topk_w;
@@ -890,6 +906,43 @@ int launch_any(int64_t n_rows, int E, const void* act, const int32_t* offsets, i
                                               group_size, sorted_slots, topk_w, out, st, ep);
   return launch_tc<GEMM1, BITS, FAST, 64>(act, n_rows, offsets, E, K, rows_total, inter, n_out, q, scale,
                                           group_size, sorted_slots, topk_w, out, st, ep);
+}
+
+// out[m, n] = bf16(sum over slices s, in order, of partial[s][m][n])
+__global__ void splitk_reduce_kernel(const float4* __restrict__ partial, int ksplit, int64_t n4,
+                                     uint2* __restrict__ out) {
+  pdl_wait();
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float4 acc = __ldg(partial + i);
+    for (int s = 1; s < ksplit; ++s) {
+      const float4 v = __ldg(partial + static_cast<int64_t>(s) * n4 + i);
+      acc.x = __fadd_rn(acc.x, v.x);
+      acc.y = __fadd_rn(acc.y, v.y);
+      acc.z = __fadd_rn(acc.z, v.z);
+      acc.w = __fadd_rn(acc.w, v.w);
+    }
+    __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
+    __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
+    uint2 o;
+    o.x = *reinterpret_cast<uint32_t*>(&lo);
+    o.y = *reinterpret_cast<uint32_t*>(&hi);
+    out[i] = o;
+  }
+}
+
+template <int BITS, int NTM>
+int dense_tc(const void* x, int64_t M, int K, int N, const int8_t* q, const float* scale, int group_size, void* out,
+             int ksplit, float* partial, cudaStream_t st) {
+  int rc = launch_tc<false, BITS, false, NTM>(x, M, nullptr, 1, K, N, 0, N, q, scale, group_size, nullptr, nullptr,
+                                              out, st, nullptr, ksplit, partial);
+  if (rc || ksplit == 1) return rc;
+  const int64_t n4 = M * N / 4;
+  int64_t blocks = (n4 + 255) / 256;
+  if (blocks > static_cast<int64_t>(num_sms()) * 8) blocks = static_cast<int64_t>(num_sms()) * 8;
+  launch_pdl(splitk_reduce_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st,
+             reinterpret_cast<const float4*>(partial), ksplit, n4, static_cast<uint2*>(out));
+  return check_launch("splitk_reduce_kernel");
 }
 
 }  // namespace
@@ -948,3 +1001,36 @@ extern "C" int llq_trace_read(long long* host) {
   return cudaMemcpyFromSymbol(host, llq::g_tc_trace, sizeof(long long) * 8 * 64) == cudaSuccess ? 0 : 3;
 }
 #endif
+
+namespace llq {
+
+// K slices for a dense layer: enough work items to cover the SMs, each slice a
+// whole number of 128-wide K steps
+int dense_ksplit(int64_t M, int K, int N) {
+  const int ntm = M > 96 ? 128 : 64;
+  const int64_t items = (M + ntm - 1) / ntm * (N / (2 * ROWS));
+  const int kch = K / KC;
+  int ks = 1;
+  while (items * ks * 2 <= num_sms() && kch % (ks * 2) == 0) ks *= 2;
+  return ks;
+}
+
+int dense_linear_tc(const void* x, int64_t M, int K, int N, const int8_t* q, const float* scale, int bits,
+                    int group_size, void* out, void* workspace, size_t ws_bytes, cudaStream_t st) {
+  if (!tc_supported(1, N, K, bits, group_size, false))
+    return fail(LLQ_EUNSUPPORTED, "tcgen05 dense linear needs K %% 128 == 0, K <= 2048, N %% 256 == 0 and "
+                                  "group %% 128 == 0 (K=%d N=%d group=%d)", K, N, group_size);
+  const int ks = dense_ksplit(M, K, N);
+  const size_t need = ks > 1 ? static_cast<size_t>(ks) * M * N * 4 : 0;
+  if (ks > 1 && (workspace == nullptr || ws_bytes < need))
+    return fail(LLQ_ENOSPACE, "quant_linear workspace needs %zu bytes, got %zu", need, ws_bytes);
+  float* partial = static_cast<float*>(workspace);
+  if (M > 96) {
+    return bits == 4 ? dense_tc<4, 128>(x, M, K, N, q, scale, group_size, out, ks, partial, st)
+                     : dense_tc<8, 128>(x, M, K, N, q, scale, group_size, out, ks, partial, st);
+  }
+  return bits == 4 ? dense_tc<4, 64>(x, M, K, N, q, scale, group_size, out, ks, partial, st)
+                   : dense_tc<8, 64>(x, M, K, N, q, scale, group_size, out, ks, partial, st);
+}
+
+}  // namespace llq

@@ -410,10 +410,26 @@ def _quant_linear_impl(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tens
     M, K = x.shape
     N = qweight.shape[0]
     out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
-    check(load().llq_quant_linear(x.data_ptr(), M, K, N, qweight.data_ptr(), scale.data_ptr(), bits,
-                                  _group_of(qweight, scale, bits), out.data_ptr(), 0, _stream(x)),
+    lib = load()
+    need = lib.llq_quant_linear_workspace_size(M, K, N)
+    ws = _linear_workspace(need, x.device) if need else None
+    check(lib.llq_quant_linear(x.data_ptr(), M, K, N, qweight.data_ptr(), scale.data_ptr(), bits,
+                               _group_of(qweight, scale, bits), out.data_ptr(),
+                               ws.data_ptr() if ws is not None else None, need, 0, _stream(x)),
           "quant_linear")
     return out
+
+
+_LIN_WS: dict = {}
+
+
+def _linear_workspace(nbytes: int, device) -> torch.Tensor:
+    key = str(device)
+    ws = _LIN_WS.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        _LIN_WS[key] = ws
+    return ws
 
 
 quant_linear = torch.library.custom_op("llada_quant::quant_linear", mutates_args=())(_quant_linear_impl)
