@@ -152,21 +152,39 @@ def _cpu_case():
 
 
 def cpu_reference(sample_layers: int = 1, threads=None):
-    """Time the reference CPU path (numpy port, oracle/moe.py) on a bounded sample:
-    ``sample_layers`` C3 layer calls of 256 tokens, each dequantizing every expert (what
-    the PACKED property does) and running the routed dequant-then-matmul.
-    Returns (tokens/s, cores, seconds)."""
+    """Time the reference CPU path on a bounded sample: ``sample_layers`` C3 layer calls of
+    256 tokens, each dequantizing every expert (what the PACKED property does) and running
+    the routed dequant-then-matmul.  With the unmodified reference installed in
+    baseline/_ref this is its own ``dequantize_tensor`` in torch on the host cores plus the
+    routed restatement (kind "reference"); otherwise the numpy port (kind "port").
+    Returns (tokens/s, cores, seconds, kind)."""
     from threadpoolctl import threadpool_limits
-    from oracle import moe as M
-
     c = _cpu_case()
     cores = threads or os.cpu_count()
+    pkg = _reference_package()
+    if pkg is not None:
+        import torch
+        RS = pkg[0]
+        torch.set_num_threads(cores)
+        if "torch" not in c:
+            from llada_quant_b200.moe import PackedExperts
+            c["torch"] = (torch.from_numpy(c["x"]).to(torch.bfloat16), torch.from_numpy(c["gate_w"]).to(torch.bfloat16),
+                          PackedExperts(torch.from_numpy(c["q1"]), torch.from_numpy(c["s1"]),
+                                        torch.from_numpy(c["q2"]), torch.from_numpy(c["s2"]), BITS, GROUP))
+        x, gate_w, layer = c["torch"]
+        deq = lambda q, sc: RS.dequantize_tensor(q, sc, BITS, GROUP, dtype=torch.bfloat16, packed=True)
+        t0 = time.perf_counter()
+        for _ in range(sample_layers):
+            _ref_layer(x, gate_w, layer, False, deq)
+        dt = time.perf_counter() - t0
+        return sample_layers * T_PER_RANK / dt, cores, dt, "reference"
+    from oracle import moe as M
     with threadpool_limits(limits=cores):
         t0 = time.perf_counter()
         for _ in range(sample_layers):
             M.moe_layer(c["x"], c["gate_w"], c["q1"], c["s1"], c["q2"], c["s2"], TOPK, BITS)
         dt = time.perf_counter() - t0
-    return sample_layers * T_PER_RANK / dt, cores, dt
+    return sample_layers * T_PER_RANK / dt, cores, dt, "port"
 
 
 def run_reference(args, rank: int):
@@ -178,8 +196,9 @@ def run_reference(args, rank: int):
     for _ in range(min(args.warmup, 1)):
         cpu_reference(1)
     cores = os.cpu_count()
+    kind = "port"
     for _ in range(args.steps):
-        v, cores, dt = cpu_reference(1)
+        v, cores, dt, kind = cpu_reference(1)
         vals.append(v)
     value = statistics.median(vals)
     line = {
@@ -189,9 +208,11 @@ def run_reference(args, rank: int):
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) tokens)", "impl": "reference",
         "config": {"workload": "C3 LLaDA-MoE-7B-A1B layer: E=64 H=2048 I=1024 top-8 W4A16 g128",
                    "tokens_per_step": T_PER_RANK},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": "one C3 layer call (256 tokens) per step: numpy port of the "
-                                   "reference's PACKED dequantize + routed dequant-then-matmul"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
+                         "sample": "one C3 layer call (256 tokens) per step: "
+                                   + ("the reference's own dequantize_tensor (baseline/_ref) in torch on the host"
+                                      " cores + the routed dequant-then-matmul" if kind == "reference" else
+                                      "numpy port of the reference's PACKED dequantize + routed dequant-then-matmul")},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -234,15 +255,32 @@ def _ref_dequantize(q, s, bits: int):
     return w.reshape(v.shape).to(torch.bfloat16)
 
 
-def _ref_layer(x, gate_w, layer, grouped: bool):
-    """The reference PACKED forward on the GPU: block.w1/w2 dequantized afresh (runtime/moe.py:
-    199-216), router softmax(fp32).topk (trajectory/llada.py:225-234), and the routed FFN in
-    the fused_moe rounding order (INFERENCE_REPO_CHANGES.md:259-265, 296-309) as BF16
-    matmuls (torch._grouped_mm, or one matmul per expert)."""
+def _reference_package():
+    """The unmodified reference installed in baseline/_ref (pip --target), when present."""
+    path = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(path):
+        return None
+    if path not in sys.path:
+        sys.path.insert(0, path)
+    try:
+        from LLaDA_Quant.algorithms import symmetric as RS
+        from LLaDA_Quant.runtime import moe as RM
+        from LLaDA_Quant.runtime.kernels import w8a16_gemm as RK
+        return RS, RM, RK
+    except Exception:
+        return None
+
+
+def _ref_layer(x, gate_w, layer, grouped: bool, deq):
+    """The reference PACKED forward on the GPU: block.w1/w2 dequantized afresh by ``deq``
+    (the PACKED property, runtime/moe.py:199-216), router softmax(fp32).topk
+    (trajectory/llada.py:225-234), and the routed FFN in the fused_moe rounding order
+    (INFERENCE_REPO_CHANGES.md:259-265, 296-309) as BF16 matmuls (torch._grouped_mm, or
+    one matmul per expert)."""
     import torch
     import torch.nn.functional as F
-    W1 = _ref_dequantize(layer.qw1, layer.sw1, BITS)
-    W2 = _ref_dequantize(layer.qw2, layer.sw2, BITS)
+    W1 = deq(layer.qw1, layer.sw1)
+    W2 = deq(layer.qw2, layer.sw2)
     probs = F.softmax(F.linear(x, gate_w), dim=-1, dtype=torch.float32)
     tw, ti = probs.topk(TOPK, dim=-1)
     flat = ti.reshape(-1)
@@ -277,36 +315,95 @@ def _ref_layer(x, gate_w, layer, grouped: bool):
     return slots.view(-1, TOPK, H).float().sum(dim=1).to(torch.bfloat16)
 
 
-def time_gpu_reference(xs, gate_w, layers, args, device):
-    """The reference algorithm on the same B200, timed like our device value."""
+def _time_ref(fn, steps):
     import torch
-    grouped = True
-    try:
-        _ref_layer(xs[0], gate_w, layers[0], True)
-        torch.cuda.synchronize()
-    except Exception:
-        grouped = False
-    for i in range(max(2, min(args.warmup, 3))):
-        _ref_layer(xs[i % N_LAYERS], gate_w, layers[i % N_LAYERS], grouped)
-    torch.cuda.synchronize()
-    steps = max(3, min(args.steps, 10))
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
     for i in range(steps):
-        _ref_layer(xs[i % N_LAYERS], gate_w, layers[i % N_LAYERS], grouped)
+        fn(i)
     e.record()
     torch.cuda.synchronize()
-    ms = s.elapsed_time(e) / steps
+    return s.elapsed_time(e) / steps
+
+
+def time_gpu_reference(xs, gate_w, layers, args, device):
+    """The reference algorithm on the same B200, timed like our device value: the
+    reference's own dequantize_tensor (eager, and its torch.compile'd variant) from
+    baseline/_ref when installed, else its restatement in torch ops."""
+    import torch
+    pkg = _reference_package()
+    if pkg is not None:
+        RS, RM, _ = pkg
+        eager = lambda q, sc: RS.dequantize_tensor(q, sc, BITS, GROUP, dtype=torch.bfloat16, packed=True)
+        source = "baseline/_ref (unmodified LLaDA_Quant package): dequantize_tensor"
+    else:
+        eager = lambda q, sc: _ref_dequantize(q, sc, BITS)
+        source = "restatement of dequantize_tensor in torch ops (baseline/_ref not installed)"
+    grouped = True
+    try:
+        _ref_layer(xs[0], gate_w, layers[0], True, eager)
+        torch.cuda.synchronize()
+    except Exception:
+        grouped = False
+    steps = max(3, min(args.steps, 10))
+    out = {}
+    variants = [("eager", eager)]
+    if pkg is not None:
+        comp = RM.compiled_dequantize()
+        variants.append(("compiled", lambda q, sc: comp(q, sc, BITS, GROUP, dtype=torch.bfloat16, packed=True)))
+    for name, deq in variants:
+        try:
+            for i in range(max(2, min(args.warmup, 3))):
+                _ref_layer(xs[i % N_LAYERS], gate_w, layers[i % N_LAYERS], grouped, deq)
+            torch.cuda.synchronize()
+            ms = _time_ref(lambda i: _ref_layer(xs[i % N_LAYERS], gate_w, layers[i % N_LAYERS], grouped, deq), steps)
+            out[name] = {"value": T_PER_RANK / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "steps": steps}
+        except Exception as exc:  # a failing baseline leg is reported, never hidden
+            out[name] = {"error": f"{type(exc).__name__}: {exc}"[:200]}
     from llada_quant_b200 import ops
-    ref = _ref_layer(xs[0], gate_w, layers[0], grouped).float()
+    ref = _ref_layer(xs[0], gate_w, layers[0], grouped, eager).float()
     tw, ids, _ = ops._route_impl(xs[0], gate_w, TOPK, None, False)
     ours = ops._fused_moe_packed_impl(xs[0], layers[0].qw1, layers[0].sw1, layers[0].qw2, layers[0].sw2, tw, ids,
                                       BITS, 0).float()
-    rel = float((ours - ref).norm() / ref.norm())
-    return {"value": T_PER_RANK / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "steps": steps,
-            "rel_l2_vs_ours": rel,
-            "method": "reference PACKED path on this GPU: dequantize_tensor of w1/w2 to bf16 per call + "
-                      + ("torch._grouped_mm" if grouped else "per-expert torch matmul") + " (bf16)"}
+    best = min((v for v in out.values() if "value" in v), key=lambda v: v["ms_per_step"], default=None)
+    line = {"source": source,
+            "method": "PACKED dequantize of w1/w2 to bf16 per call + "
+                      + ("torch._grouped_mm" if grouped else "per-expert torch matmul") + " (bf16)",
+            "rel_l2_vs_ours": float((ours - ref).norm() / ref.norm()), "variants": out}
+    if best is not None:
+        line.update(value=best["value"], unit=UNIT, ms_per_step=best["ms_per_step"])
+    return line
+
+
+def time_w8a16_comparator(device):
+    """The reference's Triton w8a16_gemm (runtime/kernels/w8a16_gemm.py:74-85) against this
+    package's dense W8A16 kernel on the same plain GEMM (K=2048, N=8192, 16 MiB of int8
+    weights, 12 rotated copies so that no call reads weights left in L2)."""
+    import torch
+    pkg = _reference_package()
+    if pkg is None or not pkg[2].HAS_TRITON:
+        return {"unavailable": "baseline/_ref with Triton is not installed"}
+    RK = pkg[2]
+    from llada_quant_b200 import ops
+    K, N, copies = 2048, 8192, 12
+    g = torch.Generator(device=device).manual_seed(7)
+    ws = [torch.randint(-127, 128, (N, K), generator=g, device=device, dtype=torch.int8) for _ in range(copies)]
+    ss = [torch.rand(N, K // 128, generator=g, device=device) * 0.01 for _ in range(copies)]
+    rows = []
+    for M in (16, 64, 128, 256):
+        a = torch.randn(M, K, generator=g, device=device).to(torch.bfloat16)
+        for i in range(3):
+            RK.w8a16_gemm(a, ws[i], ss[i])
+            ops._quant_linear_impl(a, ws[i], ss[i], 8)
+        torch.cuda.synchronize()
+        t_ref = _time_ref(lambda i: RK.w8a16_gemm(a, ws[i % copies], ss[i % copies]), 24)
+        t_ours = _time_ref(lambda i: ops._quant_linear_impl(a, ws[i % copies], ss[i % copies], 8), 24)
+        y_ref = RK.w8a16_gemm(a, ws[0], ss[0]).float()
+        y_ours = ops._quant_linear_impl(a, ws[0], ss[0], 8).float()
+        rows.append({"M": M, "reference_triton_us": round(t_ref * 1e3, 2), "ours_us": round(t_ours * 1e3, 2),
+                     "rel_l2": float((y_ours - y_ref).norm() / y_ref.norm())})
+    return {"shape": {"K": K, "N": N, "bits": 8, "group": 128}, "rows": rows,
+            "note": "per call, host-launched (both sides pay their launch overhead)"}
 
 
 def run_ours(args, rank: int, world: int, local_rank: int):
@@ -436,16 +533,20 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         kernel["layer"] = {"algorithmic_bytes": layer_algo, "achieved": round(layer_gbs, 1),
                            "frac": round(layer_gbs / peak, 4)}
 
-    gpu_ref = None
+    gpu_ref = w8a16 = None
     if world == 1 and not args.no_gpu_ref:
         gpu_ref = time_gpu_reference(xs, gate_w, layers, args, device)
+        w8a16 = time_w8a16_comparator(device)
 
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu:
-            v, cores, dt = cpu_reference(1)
-            cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
-                   "sample": f"one C3 layer call (256 tokens) of the numpy port of the reference CPU path, {dt:.1f} s"}
+            cpu_reference(1)  # warm-up: page in, thread pools
+            v, cores, dt, kind = cpu_reference(1)
+            cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": kind,
+                   "sample": f"one C3 layer call (256 tokens), {dt:.2f} s: "
+                             + ("the reference's own dequantize_tensor (baseline/_ref) in torch + routed matmul"
+                                if kind == "reference" else "numpy port of the reference CPU path")}
         # ours per step: router, align, permute, GEMM1, GEMM2, combine; at N > 1 over the
         # window: router, dispatch, align, permute, GEMM1, GEMM2, combine; over NCCL: router,
         # rank grouping, pack, align, permute, GEMM1, GEMM2, combine, slot combine
@@ -469,6 +570,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         }
         if gpu_ref is not None:
             line["gpu_reference"] = gpu_ref
+        if w8a16 is not None:
+            line["gpu_reference_w8a16_gemm"] = w8a16
         print(json.dumps(line), flush=True)
     if window is not None:
         window.close()
