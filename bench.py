@@ -426,6 +426,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     g = torch.Generator(device=device).manual_seed(2 + rank)
     xs = [torch.randn(T_PER_RANK, H, generator=g, device=device).to(torch.bfloat16) for _ in range(N_LAYERS)]
     bias = None
+    if args.router_bias == "zipf":
+        # C5 skew: b_e = -1.1 ln(rank_e), rank_e a seeded permutation of 1..E
+        rank_e = torch.randperm(E, generator=torch.Generator().manual_seed(3)).to(torch.float32) + 1.0
+        bias = (-1.1 * torch.log(rank_e)).to(device)
     window = None
     if world > 1 and args.ep_transport == "window":
         window = ep.EPWindow(T_PER_RANK, TOPK, H, rank, world, device)
@@ -474,9 +478,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         x = x_host[i % N_LAYERS].to(device, non_blocking=True)
         if world > 1:
             from llada_quant_b200 import ep
-            out = ep.ep_moe_layer(x, gate_w, layers[i % N_LAYERS], TOPK, rank, world, impl=impl, window=window)
+            out = ep.ep_moe_layer(x, gate_w, layers[i % N_LAYERS], TOPK, rank, world, bias=bias, impl=impl,
+                                  window=window)
         else:
-            out = moe_layer(x, gate_w, layers[i % N_LAYERS], TOPK, impl=args.gemm)
+            out = moe_layer(x, gate_w, layers[i % N_LAYERS], TOPK, bias=bias, impl=args.gemm)
         out_host.copy_(out, non_blocking=True)
 
     for i in range(args.warmup):
@@ -502,7 +507,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     if world == 1:
         preps = []
         for l in range(N_LAYERS):
-            tw, ids, _ = ops.route(xs[l], gate_w, TOPK, None, False)
+            tw, ids, _ = ops.route(xs[l], gate_w, TOPK, bias, False)
             offsets, slots = ops.moe_align(ids, E)
             xsrt = ops.moe_permute(xs[l], slots, TOPK, args.gemm == "tcgen05_fast")
             hit = int((offsets[1:] - offsets[:-1] > 0).sum().item())
@@ -560,6 +565,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                        "tokens_per_rank": T_PER_RANK, "gemm": args.gemm,
                        "parallelism": "ep%d" % world if world > 1 else "single",
                        "ep_transport": (args.ep_transport if world > 1 else None),
+                       "router_bias": args.router_bias,
                        "l2": "inputs larger than L2: 4 rotated layer weight sets (4 x 214 MB)"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T_PER_RANK * H * 2,
                     "d2h_bytes_per_step": T_PER_RANK * H * 2},
@@ -678,6 +684,8 @@ def main():
                     help="skip the reference-algorithm-on-B200 leg (dequantize + BF16 matmul)")
     ap.add_argument("--ep-transport", choices=["window", "nccl"], default="window",
                     help="expert-parallel row exchange at N > 1")
+    ap.add_argument("--router-bias", choices=["none", "zipf"], default="none",
+                    help="zipf: the C5 per-expert router bias -1.1 ln(rank_e) (skewed expert load)")
     ap.add_argument("--workload", choices=["c3", "c4"], default="c3",
                     help="c3: one LLaDA-MoE layer at 256 tokens (default, HBM-bound); c4: the 16-layer "
                          "stack over batch 32 x seq 1024 tokens (tensor-bound)")

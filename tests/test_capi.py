@@ -57,3 +57,41 @@ def test_argument_validation_needs_no_gpu():
     assert rc == _lib.LLQ_EINVAL and b"max_shrink" in lib.llq_last_error()
     rc = lib.llq_fused_moe_packed(*([None] * 7), 4, 8, 64, 32, 2, 4, 128, None, None, 0, 0, None)
     assert rc == _lib.LLQ_ENOSPACE
+
+
+def _a256(v):
+    return (v + 255) // 256 * 256
+
+
+def test_ep_window_layout_and_validation_need_no_gpu():
+    """The exchange window holds the signal words, the received (id, weight) pairs and the
+    received / returned rows of every rank, each 256-byte aligned."""
+    lib = _lib.load()
+    R, cap, H = 8, 2048, 2048
+    expect = _a256(4 * (5 * R + 8)) + 2 * _a256(4 * R * cap) + 2 * _a256(R * cap * H * 2)
+    assert lib.llq_ep_window_bytes(R, cap, H) == expect
+    assert lib.llq_ep_window_bytes(0, cap, H) == 0
+    assert lib.llq_ipc_handle_bytes() == 64
+    # T*k beyond the window capacity, bad world/rank: rejected before any launch
+    rc = lib.llq_ep_dispatch(1, 1, 1, 300, 8, H, 8, 1, 1, 0, 8, 2048, 1, 1, None)
+    assert rc == _lib.LLQ_EINVAL and b"exceeds the window capacity" in lib.llq_last_error()
+    rc = lib.llq_ep_dispatch(1, 1, 1, 1, 8, H, 8, 1, 1, 3, 2, 2048, 1, 1, None)
+    assert rc == _lib.LLQ_EINVAL and b"rank 3" in lib.llq_last_error()
+    rc = lib.llq_ep_experts(1, 1, 0, 2, 2048, 1, 1, 1, 1, 1, 32, H, 1024, 4, 128, 2048, 1, 1 << 30,
+                            _lib.LLQ_GEMM_SIMT, None)
+    assert rc == _lib.LLQ_EUNSUPPORTED
+    assert lib.llq_ep_set_timeout_ms(0) == _lib.LLQ_EINVAL
+
+
+def test_quant_linear_validation_needs_no_gpu():
+    lib = _lib.load()
+    rc = lib.llq_quant_linear(1, 4, 1024, 256, 1, 1, 3, 128, 1, None, 0, 0, None)
+    assert rc == _lib.LLQ_EUNSUPPORTED and b"bits must be 8 or 4" in lib.llq_last_error()
+    rc = lib.llq_quant_linear(1, 4, 1023, 256, 1, 1, 4, 128, 1, None, 0, 0, None)
+    assert rc == _lib.LLQ_EINVAL and b"even last dimension" in lib.llq_last_error()
+    rc = lib.llq_quant_linear(1, 4, 1024, 256, 1, 1, 4, 128, 1, None, 0, _lib.LLQ_GEMM_TCGEN05_FAST, None)
+    assert rc == _lib.LLQ_EUNSUPPORTED
+    assert lib.llq_quant_linear(None, 0, 1024, 256, None, None, 4, 128, None, None, 0, 0, None) == _lib.LLQ_OK
+    # one 1-token row of a 2048 x 2048 layer is 8 output tiles: split K so that the SMs are covered
+    assert lib.llq_quant_linear_workspace_size(1, 2048, 2048) % (2048 * 4) == 0
+    assert lib.llq_quant_linear_workspace_size(1, 2048, 2048) >= 2 * 2048 * 4
