@@ -42,6 +42,8 @@ struct MoeWorkspace {
   void* x_sorted;
   void* h_sorted;
   void* y_slots;
+  int32_t* tile_done;
+  int tile_done_n;
   size_t total;
 };
 
@@ -61,8 +63,19 @@ MoeWorkspace carve(void* base, int64_t T, int k, int E, int H, int I) {
   w.x_sorted = take(static_cast<size_t>(n) * H * 2 + 4096);
   w.h_sorted = take(static_cast<size_t>(n) * I * 2 + 4096);
   w.y_slots = take(static_cast<size_t>(n) * H * 2 + 4096);
+  w.tile_done_n = static_cast<int>(n / 16 + E + 1);  // token tiles are >= 64 rows, one partial tile per expert
+  w.tile_done = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * w.tile_done_n));
   w.total = off;
   return w;
+}
+
+// LLQ_FUSED_GEMMS=0 runs GEMM1 and GEMM2 as two launches (development A/B switch)
+bool fused_gemms() {
+  static const bool on = [] {
+    const char* e = getenv("LLQ_FUSED_GEMMS");
+    return e == nullptr || atoi(e) != 0;
+  }();
+  return on;
 }
 
 int pick_impl(int impl, int E, int N_out, int K, int bits, int group_size, bool gemm1) {
@@ -211,7 +224,10 @@ int llq_fused_moe_packed(const void* x, const int8_t* qw1, const float* sw1, con
     return fail(LLQ_ENOSPACE, "workspace needs %zu bytes, got %zu", ws.total, workspace_bytes);
   cudaStream_t st = as_stream(stream);
   const int64_t n = T * k;
-  int rc = align_impl(topk_ids, T, k, E, ws.offsets, ws.sorted_slots, ws.align_ws, ws.align_bytes, st);
+  AlignMask am{};
+  am.clear = ws.tile_done;
+  am.clear_n = ws.tile_done_n;
+  int rc = align_impl_masked(topk_ids, n, E, ws.offsets, ws.sorted_slots, ws.align_ws, ws.align_bytes, st, am);
   if (rc) return rc;
   if (impl == LLQ_GEMM_TCGEN05_FAST) {
     if (pick_impl(impl, E, I, H, bits, group_size, true) < 0 ||
@@ -229,6 +245,13 @@ int llq_fused_moe_packed(const void* x, const int8_t* qw1, const float* sw1, con
   }
   rc = permute_impl(x, T, H, k, ws.sorted_slots, ws.x_sorted, st, 0);
   if (rc) return rc;
+  if (fused_gemms() && pick_impl(impl, E, I, H, bits, group_size, true) == LLQ_GEMM_TCGEN05 &&
+      pick_impl(impl, E, H, I, bits, group_size, false) == LLQ_GEMM_TCGEN05) {
+    rc = gemm12_fused_tc(ws.x_sorted, ws.offsets, ws.sorted_slots, topk_w, n, E, H, I, qw1, sw1, qw2, sw2, bits,
+                         group_size, ws.h_sorted, ws.y_slots, ws.tile_done, st);
+    if (rc) return rc;
+    return combine_impl(ws.y_slots, T, k, H, out, st);
+  }
   rc = llq_moe_gemm1(ws.x_sorted, ws.offsets, n, E, H, I, qw1, sw1, bits, group_size, ws.h_sorted,
                      impl, stream);
   if (rc) return rc;

@@ -70,6 +70,12 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -112,6 +118,8 @@ struct AlignMask {
   int R;
   uint32_t epoch;
   uint64_t timeout_ns;
+  int32_t* clear;          // optional: zeroed by the alignment (the fused GEMMs' tile counters)
+  int clear_n;
 };
 
 // Scatter target of the expert GEMM2 in expert-parallel mode: the output row of

@@ -35,6 +35,10 @@ int gemm2_tc(const void*, const int32_t*, const int32_t*, const float*, int64_t,
 bool tc_supported(int E, int N_out, int K, int bits, int group_size, bool gemm1);
 
 int dense_ksplit(int64_t M, int K, int N);
+int gemm12_fused_tc(const void* x_sorted, const int32_t* offsets, const int32_t* sorted_slots, const float* topk_w,
+                    int64_t n_rows, int E, int H, int I, const int8_t* qw1, const float* sw1, const int8_t* qw2,
+                    const float* sw2, int bits, int group_size, void* h_sorted, void* y_slots, int* tile_done,
+                    cudaStream_t st);
 int dense_linear_tc(const void* x, int64_t M, int K, int N, const int8_t* q, const float* scale, int bits,
                     int group_size, void* out, void* workspace, size_t ws_bytes, cudaStream_t st);
 int align_impl_masked(const int32_t*, int64_t, int, int32_t*, int32_t*, void*, size_t, cudaStream_t,

@@ -109,20 +109,27 @@ struct Cfg {
   static_assert(!FAST || BITS == 4, "fast mode is INT4 only");
 };
 
-struct TcArgs {
-  const int32_t* offsets;
+// one GEMM of the kernel (GEMM1 or GEMM2): its weights' scales, output and sizes
+struct TcPhase {
   const float* scale;
-  const int32_t* sorted_slots;
-  const float* topk_w;
   __nv_bfloat16* out;
-  int E;
   int K;           // reduction length (H for GEMM1, I for GEMM2)
   int rows_total;  // weight rows per expert (2I or H)
-  int inter;       // I
+  int inter;       // I (GEMM1)
   int n_out;       // output row length (I for GEMM1, H for GEMM2)
   int rblocks;     // 256-row blocks per expert (I/128 for GEMM1, H/256 for GEMM2)
   int group;       // 0 = one scale per row
   int groups;      // scales per row
+};
+
+struct TcArgs {
+  const int32_t* offsets;
+  const int32_t* sorted_slots;
+  const float* topk_w;
+  TcPhase ph[2];   // ph[0] alone, or GEMM1 then GEMM2 when `fused`
+  int fused;       // GEMM1 items, then GEMM2 items that wait for their token tile's GEMM1 items
+  int* tile_done;  // fused: per token tile, GEMM1 epilogue warps finished (zeroed by the alignment)
+  int E;
   int debug;       // development switch: 1 = no dequant math, 2 = no MMA, 4 = no TMEM stores,
                    // 8 = no token-tile loads (results are wrong)
   int dense_rows;  // offsets == nullptr: one expert of this many rows, identity slots, weight 1
@@ -365,7 +372,7 @@ __device__ __forceinline__ int box_index(int rows) {
 }
 
 struct Item {
-  int e, tt, rb, row0, rows_t, ks;
+  int e, tt, tg, rb, row0, rows_t, ks, ph;
 };
 
 // ---------------------------------------------------------------------------
@@ -373,9 +380,12 @@ struct Item {
 // ---------------------------------------------------------------------------
 template <bool GEMM1, int BITS, bool FAST, int NTM>
 __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
-    moe_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_b0,
-                       const __grid_constant__ CUtensorMap tm_b1, const __grid_constant__ CUtensorMap tm_b2,
-                       const __grid_constant__ CUtensorMap tm_b3, const TcArgs args) {
+    moe_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_b00,
+                       const __grid_constant__ CUtensorMap tm_b01, const __grid_constant__ CUtensorMap tm_b02,
+                       const __grid_constant__ CUtensorMap tm_b03, const __grid_constant__ CUtensorMap tm_w1,
+                       const __grid_constant__ CUtensorMap tm_b10, const __grid_constant__ CUtensorMap tm_b11,
+                       const __grid_constant__ CUtensorMap tm_b12, const __grid_constant__ CUtensorMap tm_b13,
+                       const TcArgs args) {
   using C = Cfg<GEMM1, BITS, FAST, NTM>;
   constexpr int S = C::STAGES;
   constexpr int AS = C::A_STAGES;
@@ -404,9 +414,9 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = args.E;
-  const int G = args.groups;
   pdl_wait();
-  const int kch = args.K / KC;
+  // phase of an item: 0 = GEMM1 (or the single GEMM), 1 = GEMM2 of a fused launch
+  auto is_g1 = [&](int ph) -> bool { return args.fused ? ph == 0 : GEMM1; };
 
   // ---- compacted work list: token tiles per expert, prefix-summed by warp 0
   if (warp == 0) {
@@ -466,15 +476,20 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int total_tiles = tile_prefix[E];
-  const int total_items = total_tiles * args.rblocks * args.ksplit;
-  const int kper = kch / args.ksplit;  // K steps per item
+  const int items0 = total_tiles * args.ph[0].rblocks * args.ksplit;
+  const int total_items = items0 + (args.fused ? total_tiles * args.ph[1].rblocks : 0);
 
   auto item_at = [&](int u) -> Item {
     Item it;
-    const int uu = u / args.ksplit;
-    it.ks = u - uu * args.ksplit;
-    const int tg = uu / args.rblocks;
-    it.rb = uu - tg * args.rblocks;
+    it.ph = u >= items0 ? 1 : 0;
+    const int ks = it.ph ? 1 : args.ksplit;
+    const int v = it.ph ? u - items0 : u;
+    const int uu = v / ks;
+    it.ks = v - uu * ks;
+    const int rbl = args.ph[it.ph].rblocks;
+    const int tg = uu / rbl;
+    it.tg = tg;
+    it.rb = uu - tg * rbl;
     int lo = 0, hi = E;  // largest e with tile_prefix[e] <= tg
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
@@ -489,10 +504,16 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     return it;
   };
   auto wrow_of = [&](const Item& it, int tile) -> int64_t {
-    if (GEMM1)
-      return static_cast<int64_t>(it.e) * args.rows_total + (tile ? args.inter : 0) +
-             static_cast<int64_t>(it.rb) * ROWS;
-    return static_cast<int64_t>(it.e) * args.rows_total + static_cast<int64_t>(it.rb) * 2 * ROWS + tile * ROWS;
+    const TcPhase& P = args.ph[it.ph];
+    if (is_g1(it.ph))
+      return static_cast<int64_t>(it.e) * P.rows_total + (tile ? P.inter : 0) + static_cast<int64_t>(it.rb) * ROWS;
+    return static_cast<int64_t>(it.e) * P.rows_total + static_cast<int64_t>(it.rb) * 2 * ROWS + tile * ROWS;
+  };
+  // K steps of an item: [kbeg, kbeg + kper)
+  auto k_range = [&](const Item& it, int& kbeg, int& kper) {
+    const int kch = args.ph[it.ph].K / KC;
+    kper = kch / (it.ph ? 1 : args.ksplit);
+    kbeg = it.ks * kper;
   };
 
   if (warp == 0) {
@@ -502,26 +523,50 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
       bool ok = true;
       for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
         const Item item = item_at(u);
+        const TcPhase& P = args.ph[item.ph];
+        const int G = P.groups;
         const int sbuf = ii & 1;
         if (!mbar_wait_sleep(&sc_empty[sbuf], ((ii >> 1) & 1) ^ 1, abort_flag, 0x100)) break;
+        if (item.ph == 1) {
+          // the GEMM1 items of this token tile (every epilogue warp of each) must have stored h
+          const int need = args.ph[0].rblocks * C::EPI_WARPS;
+          const long long t0 = clock64();
+          bool ready = false;
+          while (!(ready = ld_acquire_gpu(args.tile_done + item.tg) >= need)) {
+            if (*abort_flag) break;
+            if (clock64() - t0 > kTimeoutCycles) {
+              *abort_flag = 1;
+              atomicExch(&g_device_error, 0x130);
+              break;
+            }
+            __nanosleep(64);
+          }
+          if (!ready) break;
+          asm volatile("fence.proxy.async.global;" ::: "memory");  // generic stores of h -> TMA reads
+        }
         const uint32_t sbytes = static_cast<uint32_t>(ROWS * G * 4);
         mbar_expect_tx(&sc_full[sbuf], 2 * sbytes);
         float* sdst = ssc + sbuf * (2 * ROWS * MAX_G);
-        bulk_load(sdst, args.scale + wrow_of(item, 0) * G, sbytes, &sc_full[sbuf]);
-        bulk_load(sdst + ROWS * MAX_G, args.scale + wrow_of(item, 1) * G, sbytes, &sc_full[sbuf]);
+        bulk_load(sdst, P.scale + wrow_of(item, 0) * G, sbytes, &sc_full[sbuf]);
+        bulk_load(sdst + ROWS * MAX_G, P.scale + wrow_of(item, 1) * G, sbytes, &sc_full[sbuf]);
         const int bi = box_index(item.rows_t);
         const int box = 16 << bi;
-        const CUtensorMap* tb = bi == 0 ? &tm_b0 : bi == 1 ? &tm_b1 : bi == 2 ? &tm_b2 : &tm_b3;
+        const CUtensorMap* tb =
+            item.ph == 0 ? (bi == 0 ? &tm_b00 : bi == 1 ? &tm_b01 : bi == 2 ? &tm_b02 : &tm_b03)
+                         : (bi == 0 ? &tm_b10 : bi == 1 ? &tm_b11 : bi == 2 ? &tm_b12 : &tm_b13);
+        const CUtensorMap* tw = item.ph == 0 ? &tm_w0 : &tm_w1;
         const int w0 = static_cast<int>(wrow_of(item, 0)), w1 = static_cast<int>(wrow_of(item, 1));
-        for (int kc = item.ks * kper; kc < (item.ks + 1) * kper; ++kc, ++it) {
+        int kbeg, kper;
+        k_range(item, kbeg, kper);
+        for (int kc = kbeg; kc < kbeg + kper; ++kc, ++it) {
           const int s = it % S;
           if (!mbar_wait_sleep(&wfree[s], ((it / S) & 1) ^ 1, abort_flag, 0x110 + s)) { ok = false; break; }
           if (!mbar_wait_sleep(&mdone[s], ((it / S) & 1) ^ 1, abort_flag, 0x118 + s)) { ok = false; break; }
           mbar_expect_tx(&full[s], C::W_STAGE_BYTES + ((args.debug & 8) ? 0 : 2 * box * 128));
           LLQ_TRACE_AT(0, it);
           uint8_t* wdst = sw + s * C::W_STAGE_BYTES;
-          tma_load_2d(wdst, &tm_w, kc * C::W_ROW_BYTES, w0, &full[s]);
-          tma_load_2d(wdst + C::W_TILE_BYTES, &tm_w, kc * C::W_ROW_BYTES, w1, &full[s]);
+          tma_load_2d(wdst, tw, kc * C::W_ROW_BYTES, w0, &full[s]);
+          tma_load_2d(wdst + C::W_TILE_BYTES, tw, kc * C::W_ROW_BYTES, w1, &full[s]);
           uint8_t* bdst = sb + s * C::B_STAGE_BYTES;
           if (!(args.debug & 8)) {
             tma_load_2d(bdst, tb, kc * KC, item.row0, &full[s]);
@@ -556,7 +601,9 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           if (!mbar_wait_sleep(&acc_empty[ab], ph ^ 1, abort_flag, 0x200)) break;
           tc_fence_after();
         }
-        const int kbeg = item.ks * kper, kend = kbeg + kper;
+        int kbeg, kper;
+        k_range(item, kbeg, kper);
+        const int kend = kbeg + kper;
         for (int kc = kbeg; kc < kend; ++kc, ++it) {
           const int s = it % S, sa = it % AS;
           const uint32_t acc_base = tmem + (C::ACC_BUFS == 2 ? (ii & 1) * C::ACC_BUF_COLS : 0);
@@ -606,10 +653,13 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     int it = 0;
     bool ok = true;
     for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
+      const Item item = item_at(u);
+      const TcPhase& P = args.ph[item.ph];
       const int sbuf = ii & 1;
       if (!mbar_wait(&sc_full[sbuf], (ii >> 1) & 1, abort_flag, 0x300)) break;
-      const float* srow = ssc + sbuf * (2 * ROWS * MAX_G) + wg * (ROWS * MAX_G) + r * G;
-      const int kbeg = (u % args.ksplit) * kper;
+      const float* srow = ssc + sbuf * (2 * ROWS * MAX_G) + wg * (ROWS * MAX_G) + r * P.groups;
+      int kbeg, kper;
+      k_range(item, kbeg, kper);
       for (int kc = kbeg; kc < kbeg + kper; ++kc, ++it) {
         const int s = it % S, sa = it % AS;
         if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, 0x310 + s)) { ok = false; break; }
@@ -626,7 +676,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           const int pc = BITS == 4 ? (c ^ ((r >> 1) & 3)) : (c ^ (r & 7));  // 64/128-byte swizzle
           v[ci] = *reinterpret_cast<const uint4*>(wt + pc * 16);
         }
-        const float sc = FAST ? 0.f : srow[args.group > 0 ? (kc * KC) / args.group : 0];
+        const float sc = FAST ? 0.f : srow[P.group > 0 ? (kc * KC) / P.group : 0];
         __syncwarp();
         if (lane == 0) mbar_arrive(&wfree[s]);
         // the TMEM A stage is free once the MMAs of step it - AS completed
@@ -680,22 +730,24 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     bool ok = true;
     for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
       const Item item = item_at(u);
+      const TcPhase& P = args.ph[item.ph];
+      const bool g1 = is_g1(item.ph);
       const int nt = (item.rows_t + 15) & ~15;
       const int t_begin = eg * (nt / EG), t_end = (eg + 1) * (nt / EG);
       // one token's outputs from the two fp32 accumulators of row r
       auto emit = [&](int t, float a0, float a1) {
         if (t >= t_end || t >= item.rows_t) return;
         const int64_t p = static_cast<int64_t>(item.row0) + t;
-        if (GEMM1) {
+        if (g1) {
           const float g = round_bf16(a0);
           const float up = round_bf16(a1);
           const float silu = round_bf16(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))));
           const int n = item.rb * ROWS + r;
           const int pos = FAST ? kperm_pos(n) : n;
-          args.out[p * args.n_out + pos] = __float2bfloat16_rn(__fmul_rn(silu, up));
+          P.out[p * P.n_out + pos] = __float2bfloat16_rn(__fmul_rn(silu, up));
         } else {
           if (args.ksplit > 1) {  // fp32 partial of this K slice, summed in order by splitk_reduce
-            float* prow = args.partial + (static_cast<int64_t>(item.ks) * args.dense_rows + p) * args.n_out +
+            float* prow = args.partial + (static_cast<int64_t>(item.ks) * args.dense_rows + p) * P.n_out +
                           item.rb * 2 * ROWS + r;
             prow[0] = a0;
             prow[ROWS] = a1;
@@ -707,9 +759,9 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           if (args.ep_on) {
             const int src = slot / args.ep.L.cap;
             const int64_t at = static_cast<int64_t>(args.ep.me) * args.ep.L.cap + (slot - src * args.ep.L.cap);
-            orow = reinterpret_cast<__nv_bfloat16*>(args.ep.peers[src] + args.ep.L.back) + at * args.n_out;
+            orow = reinterpret_cast<__nv_bfloat16*>(args.ep.peers[src] + args.ep.L.back) + at * P.n_out;
           } else {
-            orow = args.out + static_cast<int64_t>(slot) * args.n_out;
+            orow = P.out + static_cast<int64_t>(slot) * P.n_out;
           }
           orow += item.rb * 2 * ROWS + r;
           orow[0] = __float2bfloat16_rn(__fmul_rn(a0, w));
@@ -722,13 +774,13 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
 #pragma unroll
         for (int i = 0; i < (FAST ? HALF : 1); ++i) acc0[i] = acc1[i] = 0.f;
         if (!mbar_wait_sleep(&sc_full[sbuf], (ii >> 1) & 1, abort_flag, 0x400)) break;
-        const float* s0row = ssc + sbuf * (2 * ROWS * MAX_G) + r * G;
+        const float* s0row = ssc + sbuf * (2 * ROWS * MAX_G) + r * P.groups;
         const float* s1row = s0row + ROWS * MAX_G;
-        for (int kc = 0; kc < kch; ++kc, ++it) {
+        for (int kc = 0; kc < P.K / KC; ++kc, ++it) {
           const int pb = it & 1;
           if (!mbar_wait(&mdone[it % S], (it / S) & 1, abort_flag, 0x410 + pb)) { ok = false; break; }
           tc_fence_after();
-          const int gi = args.group > 0 ? (kc * KC) / args.group : 0;
+          const int gi = P.group > 0 ? (kc * KC) / P.group : 0;
           const float s0 = s0row[gi], s1 = s1row[gi];
           const uint32_t p0 = tmem + lane_addr + pb * 2 * NTM, p1 = p0 + NTM;
 #pragma unroll
@@ -784,6 +836,12 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[ab]);
+        if (args.fused && item.ph == 0) {
+          // this warp's rows of h are stored: count it for the token tile's GEMM2 items
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) atomicAdd(args.tile_done + item.tg, 1);
+        }
       }
     }
   }
@@ -838,18 +896,13 @@ int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t 
   return LLQ_OK;
 }
 
-template <bool GEMM1, int BITS, bool FAST, int NTM>
-int launch_tc(const void* act, int64_t n_rows, const int32_t* offsets, int E, int K, int rows_total,
-              int inter, int n_out, const int8_t* q, const float* scale, int group_size,
-              const int32_t* sorted_slots, const float* topk_w, void* out, cudaStream_t st,
-              const EpScatter* ep, int ksplit = 1, float* partial = nullptr) {
-  using C = Cfg<GEMM1, BITS, FAST, NTM>;
-  if (n_rows <= 0) return LLQ_OK;
-  CUtensorMap tw, tb[4];
+template <int BITS, int NTM>
+int phase_maps(const void* act, int64_t n_rows, int K, int E, int rows_total, const int8_t* q, CUtensorMap* tw,
+               CUtensorMap* tb) {
+  constexpr int W_ROW_BYTES = KC * BITS / 8;
   const uint64_t k_bytes = static_cast<uint64_t>(K) * BITS / 8;
-  int rc = make_map(&tw, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, k_bytes, static_cast<uint64_t>(E) * rows_total,
-                    k_bytes, C::W_ROW_BYTES, ROWS,
-                    BITS == 4 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+  int rc = make_map(tw, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, k_bytes, static_cast<uint64_t>(E) * rows_total, k_bytes,
+                    W_ROW_BYTES, ROWS, BITS == 4 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   for (int i = 0; i < 4; ++i) {
     const uint32_t box = 16u << (i < 3 || NTM >= 128 ? i : 2);
@@ -857,41 +910,104 @@ int launch_tc(const void* act, int64_t n_rows, const int32_t* offsets, int E, in
                   static_cast<uint64_t>(K) * 2, 64, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
-  TcArgs a;
-  a.offsets = offsets;
-  a.dense_rows = offsets == nullptr ? static_cast<int>(n_rows) : 0;
-  a.ksplit = ksplit;
-  a.partial = partial;
-  a.scale = scale;
-  a.sorted_slots = sorted_slots;
-  a.topk_w = topk_w;
-  a.out = static_cast<__nv_bfloat16*>(out);
-  a.E = E;
-  a.K = K;
-  a.rows_total = rows_total;
-  a.inter = inter;
-  a.n_out = n_out;
-  a.rblocks = GEMM1 ? inter / ROWS : n_out / (2 * ROWS);
+  return LLQ_OK;
+}
+
+inline TcPhase make_phase(bool gemm1, const float* scale, void* out, int K, int rows_total, int inter, int n_out,
+                          int group_size) {
+  TcPhase P;
+  P.scale = scale;
+  P.out = static_cast<__nv_bfloat16*>(out);
+  P.K = K;
+  P.rows_total = rows_total;
+  P.inter = inter;
+  P.n_out = n_out;
+  P.rblocks = gemm1 ? inter / ROWS : n_out / (2 * ROWS);
   const bool grouped = group_size > 0 && K % group_size == 0;
-  a.group = grouped ? group_size : 0;
-  a.groups = grouped ? K / group_size : 1;
-  static const int debug_flags = [] {
+  P.group = grouped ? group_size : 0;
+  P.groups = grouped ? K / group_size : 1;
+  return P;
+}
+
+inline int debug_flags() {
+  static const int flags = [] {
     const char* e = getenv("LLQ_TC_DEBUG");
     return e ? atoi(e) : 0;
   }();
-  a.debug = debug_flags;
-  a.ep_on = ep != nullptr;
-  if (ep != nullptr) a.ep = *ep;
+  return flags;
+}
+
+template <bool GEMM1, int BITS, bool FAST, int NTM>
+int launch_kernel(const CUtensorMap (&tw)[2], const CUtensorMap (&tb)[2][4], const TcArgs& a, cudaStream_t st) {
+  using C = Cfg<GEMM1, BITS, FAST, NTM>;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(moe_gemm_tc_kernel<GEMM1, BITS, FAST, NTM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(C::SMEM_BYTES));
     attr = true;
   }
-  const int grid = num_sms();
-  launch_pdl(moe_gemm_tc_kernel<GEMM1, BITS, FAST, NTM>, dim3(grid), dim3(C::THREADS), C::SMEM_BYTES, st, tw, tb[0],
-             tb[1], tb[2], tb[3], a);
+  launch_pdl(moe_gemm_tc_kernel<GEMM1, BITS, FAST, NTM>, dim3(num_sms()), dim3(C::THREADS), C::SMEM_BYTES, st,
+             tw[0], tb[0][0], tb[0][1], tb[0][2], tb[0][3], tw[1], tb[1][0], tb[1][1], tb[1][2], tb[1][3], a);
   return check_launch("moe_gemm_tc_kernel");
+}
+
+template <bool GEMM1, int BITS, bool FAST, int NTM>
+int launch_tc(const void* act, int64_t n_rows, const int32_t* offsets, int E, int K, int rows_total,
+              int inter, int n_out, const int8_t* q, const float* scale, int group_size,
+              const int32_t* sorted_slots, const float* topk_w, void* out, cudaStream_t st,
+              const EpScatter* ep, int ksplit = 1, float* partial = nullptr) {
+  if (n_rows <= 0) return LLQ_OK;
+  CUtensorMap tw[2], tb[2][4];
+  int rc = phase_maps<BITS, NTM>(act, n_rows, K, E, rows_total, q, &tw[0], tb[0]);
+  if (rc) return rc;
+  tw[1] = tw[0];
+  for (int i = 0; i < 4; ++i) tb[1][i] = tb[0][i];
+  TcArgs a{};
+  a.offsets = offsets;
+  a.dense_rows = offsets == nullptr ? static_cast<int>(n_rows) : 0;
+  a.ksplit = ksplit;
+  a.partial = partial;
+  a.sorted_slots = sorted_slots;
+  a.topk_w = topk_w;
+  a.E = E;
+  a.ph[0] = make_phase(GEMM1, scale, out, K, rows_total, inter, n_out, group_size);
+  a.ph[1] = a.ph[0];
+  a.fused = 0;
+  a.tile_done = nullptr;
+  a.debug = debug_flags();
+  a.ep_on = ep != nullptr;
+  if (ep != nullptr) a.ep = *ep;
+  return launch_kernel<GEMM1, BITS, FAST, NTM>(tw, tb, a, st);
+}
+
+// GEMM1 and GEMM2 of one layer in one persistent launch (exact mode): GEMM2 items
+// follow the GEMM1 items and start as soon as their token tile's h rows are stored
+template <int BITS, int NTM>
+int launch_fused(const void* x_sorted, void* h_sorted, int64_t n_rows, const int32_t* offsets, int E, int H, int I,
+                 const int8_t* qw1, const float* sw1, const int8_t* qw2, const float* sw2, int group_size,
+                 const int32_t* sorted_slots, const float* topk_w, void* y_slots, int* tile_done,
+                 cudaStream_t st) {
+  if (n_rows <= 0) return LLQ_OK;
+  CUtensorMap tw[2], tb[2][4];
+  int rc = phase_maps<BITS, NTM>(x_sorted, n_rows, H, E, 2 * I, qw1, &tw[0], tb[0]);
+  if (rc) return rc;
+  rc = phase_maps<BITS, NTM>(h_sorted, n_rows, I, E, H, qw2, &tw[1], tb[1]);
+  if (rc) return rc;
+  TcArgs a{};
+  a.offsets = offsets;
+  a.dense_rows = 0;
+  a.ksplit = 1;
+  a.partial = nullptr;
+  a.sorted_slots = sorted_slots;
+  a.topk_w = topk_w;
+  a.E = E;
+  a.ph[0] = make_phase(true, sw1, h_sorted, H, 2 * I, I, I, group_size);
+  a.ph[1] = make_phase(false, sw2, y_slots, I, H, 0, H, group_size);
+  a.fused = 1;
+  a.tile_done = tile_done;
+  a.debug = debug_flags();
+  a.ep_on = 0;
+  return launch_kernel<true, BITS, false, NTM>(tw, tb, a, st);
 }
 
 // decode tiles (64 tokens) unless the average expert holds more than 96 rows
@@ -992,6 +1108,24 @@ int gemm2_tc(const void* h_sorted, const int32_t* offsets, const int32_t* sorted
   }
   return launch_any<false, 8, false>(n_rows, E, h_sorted, offsets, I, H, 0, H, qw2, sw2, group_size,
                                      sorted_slots, topk_w, y_slots, st, rows_hint, ep);
+}
+
+int gemm12_fused_tc(const void* x_sorted, const int32_t* offsets, const int32_t* sorted_slots, const float* topk_w,
+                    int64_t n_rows, int E, int H, int I, const int8_t* qw1, const float* sw1, const int8_t* qw2,
+                    const float* sw2, int bits, int group_size, void* h_sorted, void* y_slots, int* tile_done,
+                    cudaStream_t st) {
+  if (!tc_supported(E, I, H, bits, group_size, true) || !tc_supported(E, H, I, bits, group_size, false))
+    return fail(LLQ_EUNSUPPORTED, "tcgen05 expert GEMMs: unsupported shape");
+  const bool wide = n_rows > static_cast<int64_t>(E) * 96;
+  if (bits == 4)
+    return wide ? launch_fused<4, 128>(x_sorted, h_sorted, n_rows, offsets, E, H, I, qw1, sw1, qw2, sw2, group_size,
+                                       sorted_slots, topk_w, y_slots, tile_done, st)
+                : launch_fused<4, 64>(x_sorted, h_sorted, n_rows, offsets, E, H, I, qw1, sw1, qw2, sw2, group_size,
+                                      sorted_slots, topk_w, y_slots, tile_done, st);
+  return wide ? launch_fused<8, 128>(x_sorted, h_sorted, n_rows, offsets, E, H, I, qw1, sw1, qw2, sw2, group_size,
+                                     sorted_slots, topk_w, y_slots, tile_done, st)
+              : launch_fused<8, 64>(x_sorted, h_sorted, n_rows, offsets, E, H, I, qw1, sw1, qw2, sw2, group_size,
+                                    sorted_slots, topk_w, y_slots, tile_done, st);
 }
 
 }  // namespace llq

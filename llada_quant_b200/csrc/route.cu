@@ -328,6 +328,8 @@ __global__ void __launch_bounds__(kAlignThreads) align_count_kernel(
   __shared__ int32_t c[kMaxExperts];
   __shared__ int32_t vc[kMaxRanks];
   for (int e = threadIdx.x; e < E; e += blockDim.x) c[e] = 0;
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < m.clear_n; i += blockDim.x) m.clear[i] = 0;
   if (m.counts != nullptr)
     for (int r = threadIdx.x; r < m.R; r += blockDim.x) vc[r] = mask_count(m, r);
   __syncthreads();
@@ -438,6 +440,7 @@ __global__ void __launch_bounds__(kAlignSmallThreads) align_small_kernel(
   __shared__ int32_t wcnt[W][kMaxExperts];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_wait();
+  for (int i = tid; i < m.clear_n; i += blockDim.x) m.clear[i] = 0;
   for (int i = tid; i < kMaxExperts; i += blockDim.x) cnt[i] = 0;
   for (int i = tid; i < W * kMaxExperts; i += blockDim.x) (&wcnt[0][0])[i] = 0;
   if (m.counts != nullptr) {
