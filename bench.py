@@ -58,6 +58,14 @@ def gemm1_bytes(n_rows: int, experts_hit: int) -> int:
     return experts_hit * ((2 * I * H // 2) + (2 * I * H // GROUP) * 4) + n_rows * H * 2 + n_rows * I * 2
 
 
+def fused_bytes(n_rows: int, experts_hit: int) -> int:
+    """Bytes the fused GEMM1+GEMM2 launch must move: packed w1, w2 and their scales for the
+    experts hit, the permuted activation rows in, the (token, slot) output rows out (h stays
+    inside the launch's L2 working set and is not counted)."""
+    per_expert = (2 * I * H // 2) + (2 * I * H // GROUP) * 4 + (H * I // 2) + (H * I // GROUP) * 4
+    return experts_hit * per_expert + n_rows * H * 2 + n_rows * H * 2
+
+
 def read_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -541,7 +549,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         ms_e2e = float(t.item())
     e2e_value = tokens_per_step / (ms_e2e / args.steps / 1e3)
 
-    # ---- dominant kernel (GEMM1) timed alone with CUDA events ----------------------
+    # ---- dominant kernel (the fused expert GEMMs) timed alone with CUDA events ---------
     kernel = None
     if world == 1:
         preps = []
@@ -550,29 +558,38 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             offsets, slots = ops.moe_align(ids, E)
             xsrt = ops.moe_permute(xs[l], slots, TOPK, args.gemm == "tcgen05_fast")
             hit = int((offsets[1:] - offsets[:-1] > 0).sum().item())
-            preps.append((xsrt, offsets, hit))
+            preps.append((xsrt, offsets, slots, tw, hit))
+        n_rows = T_PER_RANK * TOPK
+        fused = args.gemm in ("auto", "tcgen05")
+        if fused:
+            counters = ops.gemm12_counters(n_rows, E, device)
+            run = lambda l: ops._moe_gemm12_impl(preps[l][0], preps[l][1], preps[l][2], preps[l][3], layers[l].qw1,
+                                                 layers[l].sw1, layers[l].qw2, layers[l].sw2, BITS, counters)
+        else:
+            run = lambda l: ops.moe_gemm1(preps[l][0], preps[l][1], layers[l].qw1, layers[l].sw1, BITS, impl)
         for l in range(N_LAYERS):
-            ops.moe_gemm1(preps[l][0], preps[l][1], layers[l].qw1, layers[l].sw1, BITS, impl)
+            run(l)
         torch.cuda.synchronize()
         reps = max(args.steps, 8)
         ks, ke = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ks.record()
         for i in range(reps):
-            l = i % N_LAYERS
-            ops.moe_gemm1(preps[l][0], preps[l][1], layers[l].qw1, layers[l].sw1, BITS, impl)
+            run(i % N_LAYERS)
         ke.record()
         torch.cuda.synchronize()
         k_ms = ks.elapsed_time(ke) / reps
-        n_rows = T_PER_RANK * TOPK
-        hit = statistics.mean(p[2] for p in preps)
-        algo = gemm1_bytes(n_rows, int(round(hit)))
+        hit = int(round(statistics.mean(p[4] for p in preps)))
+        algo = fused_bytes(n_rows, hit) if fused else gemm1_bytes(n_rows, hit)
         peak, peak_kind = read_peaks()
         achieved = algo / (k_ms / 1e3) / 1e9
+        prof = "fused_gemms_c3.txt" if fused else ("gemm1_fast_c3.txt" if args.gemm == "tcgen05_fast"
+                                                  else "gemm1_exact_c3.txt")
         kernel = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                  "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                  "traffic": read_traffic("gemm1_fast_c3.txt" if args.gemm == "tcgen05_fast" else "gemm1_exact_c3.txt"), "kernel": "moe GEMM1 (W4A16, SiLU epilogue)",
+                  "frac": round(achieved / peak, 4), "peak_source": peak_kind, "traffic": read_traffic(prof),
+                  "kernel": ("moe GEMM1 + GEMM2 in one launch (W4A16, SiLU and routed-weight epilogues)" if fused
+                             else "moe GEMM1 (W4A16, SiLU epilogue)"),
                   "algorithmic_bytes": algo, "launch_ms": round(k_ms, 5)}
-        layer_algo = layer_bytes(T_PER_RANK, TOPK, int(round(hit)))
+        layer_algo = layer_bytes(T_PER_RANK, TOPK, hit)
         layer_gbs = layer_algo / (ms_per_step / 1e3) / 1e9
         kernel["layer"] = {"algorithmic_bytes": layer_algo, "achieved": round(layer_gbs, 1),
                            "frac": round(layer_gbs / peak, 4)}
@@ -692,7 +709,8 @@ def run_c4(args):
 
 
 def kernel_case(args):
-    """One C3 layer weight set, route -> align -> permute -> GEMM1 -> GEMM2 -> combine, twice."""
+    """One C3 layer weight set, route -> align -> permute -> fused GEMM1+GEMM2 (exact; two
+    launches in fast mode) -> combine, twice."""
     import torch
     from llada_quant_b200 import ops
     from llada_quant_b200.fused_moe import IMPL
@@ -706,8 +724,12 @@ def kernel_case(args):
         tw, ids, _ = ops.route(x, gate_w, TOPK, None, False)
         off, slots = ops.moe_align(ids, E)
         xs = ops.moe_permute(x, slots, TOPK, args.gemm == "tcgen05_fast")
-        h = ops.moe_gemm1(xs, off, lay.qw1, lay.sw1, BITS, impl)
-        y = ops.moe_gemm2(h, off, slots, tw, lay.qw2, lay.sw2, BITS, impl)
+        if args.gemm in ("auto", "tcgen05"):
+            counters = ops.gemm12_counters(T_PER_RANK * TOPK, E, device)
+            y = ops._moe_gemm12_impl(xs, off, slots, tw, lay.qw1, lay.sw1, lay.qw2, lay.sw2, BITS, counters)
+        else:
+            h = ops.moe_gemm1(xs, off, lay.qw1, lay.sw1, BITS, impl)
+            y = ops.moe_gemm2(h, off, slots, tw, lay.qw2, lay.sw2, BITS, impl)
         out = ops.moe_combine(y, TOPK)
     torch.cuda.synchronize()
     print(json.dumps({"kernel_case": "C3", "gemm": args.gemm, "out_abs_mean": float(out.float().abs().mean())}))

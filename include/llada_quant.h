@@ -245,6 +245,20 @@ int llq_quant_linear(const void* x, int64_t M, int K, int N, const int8_t* qweig
                      const float* scale, int bits, int group_size, void* out, void* workspace,
                      size_t workspace_bytes, int impl, void* stream);
 
+/*
+ * GEMM1 and GEMM2 above in one persistent launch (exact weights): the GEMM2 work
+ * of a token tile starts as soon as that tile's h rows are stored, so the two
+ * GEMMs share the SMs instead of meeting at a launch boundary.  Same arguments as
+ * the pair, plus `counters`: int32 [llq_moe_gemm12_counters(n_rows, E)] of device
+ * memory, zero-filled before the first call (every call leaves it zeroed).
+ */
+size_t llq_moe_gemm12_counters(int64_t n_rows, int E);
+int llq_moe_gemm12(const void* x_sorted, const int32_t* expert_offsets,
+                   const int32_t* sorted_slots, const float* topk_w, int64_t n_rows, int E,
+                   int H, int I, const int8_t* qw1, const float* sw1, const int8_t* qw2,
+                   const float* sw2, int bits, int group_size, void* h_sorted, void* y_slots,
+                   int32_t* counters, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Whole layer.                                                              */
 /* ------------------------------------------------------------------------ */

@@ -44,6 +44,8 @@ SIGNATURES = {
     "llq_moe_gemm2": (I, [P, P, P, P, L, I, I, I, P, P, I, I, P, I, P]),
     "llq_quant_linear_workspace_size": (c_size_t, [L, I, I]),
     "llq_quant_linear": (I, [P, L, I, I, P, P, I, I, P, P, c_size_t, I, P]),
+    "llq_moe_gemm12_counters": (c_size_t, [L, I]),
+    "llq_moe_gemm12": (I, [P, P, P, P, L, I, I, I, P, P, P, P, I, I, P, P, P, P]),
     "llq_moe_workspace_size": (c_size_t, [L, I, I, I, I]),
     "llq_fused_moe_packed": (I, [P, P, P, P, P, P, P, L, I, I, I, I, I, I, P, P, c_size_t, I, P]),
     "llq_fused_moe_packed_noalloc": (I, [P, P, P, P, P, P, P, L, I, I, I, I, I, I, P, I, P]),

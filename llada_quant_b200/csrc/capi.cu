@@ -63,7 +63,7 @@ MoeWorkspace carve(void* base, int64_t T, int k, int E, int H, int I) {
   w.x_sorted = take(static_cast<size_t>(n) * H * 2 + 4096);
   w.h_sorted = take(static_cast<size_t>(n) * I * 2 + 4096);
   w.y_slots = take(static_cast<size_t>(n) * H * 2 + 4096);
-  w.tile_done_n = static_cast<int>(n / 16 + E + 1);  // token tiles are >= 64 rows, one partial tile per expert
+  w.tile_done_n = gemm12_counter_slots(n, E);
   w.tile_done = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * w.tile_done_n));
   w.total = off;
   return w;
@@ -206,6 +206,26 @@ int llq_quant_linear(const void* x, int64_t M, int K, int N, const int8_t* qweig
   if (M > 0x7fffffff) return fail(LLQ_EINVAL, "too many rows");
   return dense_linear_tc(x, M, K, N, qweight, scale, bits, group_size, out, workspace, workspace_bytes,
                          as_stream(stream));
+}
+
+size_t llq_moe_gemm12_counters(int64_t n_rows, int E) {
+  if (n_rows < 0 || E < 1) return 0;
+  return static_cast<size_t>(gemm12_counter_slots(n_rows, E));
+}
+
+int llq_moe_gemm12(const void* x_sorted, const int32_t* expert_offsets, const int32_t* sorted_slots,
+                   const float* topk_w, int64_t n_rows, int E, int H, int I, const int8_t* qw1, const float* sw1,
+                   const int8_t* qw2, const float* sw2, int bits, int group_size, void* h_sorted, void* y_slots,
+                   int32_t* counters, void* stream) {
+  if (n_rows < 0 || E < 1 || H < 1 || I < 1) return fail(LLQ_EINVAL, "bad shape");
+  if (counters == nullptr) return fail(LLQ_EINVAL, "null counters");
+  if (n_rows == 0) return LLQ_OK;
+  if (pick_impl(LLQ_GEMM_TCGEN05, E, I, H, bits, group_size, true) < 0 ||
+      pick_impl(LLQ_GEMM_TCGEN05, E, H, I, bits, group_size, false) < 0)
+    return fail(LLQ_EUNSUPPORTED, "the fused expert GEMMs need the tcgen05 shapes (K %% 128 == 0, K <= 2048, "
+                                  "I %% 128 == 0, H %% 256 == 0, group %% 128 == 0)");
+  return gemm12_fused_tc(x_sorted, expert_offsets, sorted_slots, topk_w, n_rows, E, H, I, qw1, sw1, qw2, sw2, bits,
+                         group_size, h_sorted, y_slots, counters, as_stream(stream));
 }
 
 size_t llq_moe_workspace_size(int64_t T, int k, int E, int H, int I) {

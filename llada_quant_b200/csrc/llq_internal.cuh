@@ -35,6 +35,7 @@ int gemm2_tc(const void*, const int32_t*, const int32_t*, const float*, int64_t,
 bool tc_supported(int E, int N_out, int K, int bits, int group_size, bool gemm1);
 
 int dense_ksplit(int64_t M, int K, int N);
+int gemm12_counter_slots(int64_t n_rows, int E);
 int gemm12_fused_tc(const void* x_sorted, const int32_t* offsets, const int32_t* sorted_slots, const float* topk_w,
                     int64_t n_rows, int E, int H, int I, const int8_t* qw1, const float* sw1, const int8_t* qw2,
                     const float* sw2, int bits, int group_size, void* h_sorted, void* y_slots, int* tile_done,

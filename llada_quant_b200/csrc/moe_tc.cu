@@ -128,7 +128,8 @@ struct TcArgs {
   const float* topk_w;
   TcPhase ph[2];   // ph[0] alone, or GEMM1 then GEMM2 when `fused`
   int fused;       // GEMM1 items, then GEMM2 items that wait for their token tile's GEMM1 items
-  int* tile_done;  // fused: per token tile, GEMM1 epilogue warps finished (zeroed by the alignment)
+  int* tile_done;  // fused: per token tile, GEMM1 epilogue warps finished; [tile_done_n] then a CTA counter
+  int tile_done_n;
   int E;
   int debug;       // development switch: 1 = no dequant math, 2 = no MMA, 4 = no TMEM stores,
                    // 8 = no token-tile loads (results are wrong)
@@ -850,6 +851,16 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
   tc_fence_before();
   __syncthreads();
   pdl_trigger();
+  if (args.fused && threadIdx.x == 0) {
+    // the last CTA out leaves the tile counters zeroed for the next launch
+    int* cta_done = args.tile_done + args.tile_done_n;
+    __threadfence();
+    if (atomicAdd(cta_done, 1) == static_cast<int>(gridDim.x) - 1) {
+      for (int i = 0; i < args.tile_done_n; ++i) args.tile_done[i] = 0;
+      __threadfence();
+      atomicExch(cta_done, 0);
+    }
+  }
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
@@ -986,7 +997,7 @@ template <int BITS, int NTM>
 int launch_fused(const void* x_sorted, void* h_sorted, int64_t n_rows, const int32_t* offsets, int E, int H, int I,
                  const int8_t* qw1, const float* sw1, const int8_t* qw2, const float* sw2, int group_size,
                  const int32_t* sorted_slots, const float* topk_w, void* y_slots, int* tile_done,
-                 cudaStream_t st) {
+                 int tile_done_n, cudaStream_t st) {
   if (n_rows <= 0) return LLQ_OK;
   CUtensorMap tw[2], tb[2][4];
   int rc = phase_maps<BITS, NTM>(x_sorted, n_rows, H, E, 2 * I, qw1, &tw[0], tb[0]);
@@ -1005,6 +1016,7 @@ int launch_fused(const void* x_sorted, void* h_sorted, int64_t n_rows, const int
   a.ph[1] = make_phase(false, sw2, y_slots, I, H, 0, H, group_size);
   a.fused = 1;
   a.tile_done = tile_done;
+  a.tile_done_n = tile_done_n;
   a.debug = debug_flags();
   a.ep_on = 0;
   return launch_kernel<true, BITS, false, NTM>(tw, tb, a, st);
@@ -1110,22 +1122,26 @@ int gemm2_tc(const void* h_sorted, const int32_t* offsets, const int32_t* sorted
                                      sorted_slots, topk_w, y_slots, st, rows_hint, ep);
 }
 
+// token tiles are >= 64 rows, plus one partial tile per expert; one more slot counts CTAs
+int gemm12_counter_slots(int64_t n_rows, int E) { return static_cast<int>(n_rows / 16 + E + 2); }
+
 int gemm12_fused_tc(const void* x_sorted, const int32_t* offsets, const int32_t* sorted_slots, const float* topk_w,
                     int64_t n_rows, int E, int H, int I, const int8_t* qw1, const float* sw1, const int8_t* qw2,
                     const float* sw2, int bits, int group_size, void* h_sorted, void* y_slots, int* tile_done,
                     cudaStream_t st) {
   if (!tc_supported(E, I, H, bits, group_size, true) || !tc_supported(E, H, I, bits, group_size, false))
     return fail(LLQ_EUNSUPPORTED, "tcgen05 expert GEMMs: unsupported shape");
+  const int tile_done_n = gemm12_counter_slots(n_rows, E) - 1;
   const bool wide = n_rows > static_cast<int64_t>(E) * 96;
   if (bits == 4)
     return wide ? launch_fused<4, 128>(x_sorted, h_sorted, n_rows, offsets, E, H, I, qw1, sw1, qw2, sw2, group_size,
-                                       sorted_slots, topk_w, y_slots, tile_done, st)
+                                       sorted_slots, topk_w, y_slots, tile_done, tile_done_n, st)
                 : launch_fused<4, 64>(x_sorted, h_sorted, n_rows, offsets, E, H, I, qw1, sw1, qw2, sw2, group_size,
-                                      sorted_slots, topk_w, y_slots, tile_done, st);
+                                      sorted_slots, topk_w, y_slots, tile_done, tile_done_n, st);
   return wide ? launch_fused<8, 128>(x_sorted, h_sorted, n_rows, offsets, E, H, I, qw1, sw1, qw2, sw2, group_size,
-                                     sorted_slots, topk_w, y_slots, tile_done, st)
+                                     sorted_slots, topk_w, y_slots, tile_done, tile_done_n, st)
               : launch_fused<8, 64>(x_sorted, h_sorted, n_rows, offsets, E, H, I, qw1, sw1, qw2, sw2, group_size,
-                                    sorted_slots, topk_w, y_slots, tile_done, st);
+                                    sorted_slots, topk_w, y_slots, tile_done, tile_done_n, st);
 }
 
 }  // namespace llq

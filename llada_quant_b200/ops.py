@@ -392,6 +392,29 @@ def _(h_sorted, expert_offsets, sorted_slots, topk_w, qw2, sw2, bits, impl):
 _WS_CACHE: dict = {}
 
 
+def _moe_gemm12_impl(x_sorted: torch.Tensor, expert_offsets: torch.Tensor, sorted_slots: torch.Tensor,
+                     topk_w: torch.Tensor, qw1: torch.Tensor, sw1: torch.Tensor, qw2: torch.Tensor,
+                     sw2: torch.Tensor, bits: int, counters: torch.Tensor) -> torch.Tensor:
+    """GEMM1 (+SiLU) and GEMM2 (+routed weight) in one launch; returns y in (token, slot) order.
+    ``counters``: int32 zeros of ``llq_moe_gemm12_counters(n, E)`` (left zeroed by every call)."""
+    _need_cuda(x_sorted, expert_offsets, sorted_slots, topk_w, qw1, sw1, qw2, sw2, counters)
+    n, H = x_sorted.shape
+    E, two_i = qw1.shape[0], qw1.shape[1]
+    inter = two_i // 2
+    h = torch.empty(n, inter, dtype=torch.bfloat16, device=x_sorted.device)
+    y = torch.empty(n, H, dtype=torch.bfloat16, device=x_sorted.device)
+    tw = topk_w.contiguous().to(torch.float32)
+    check(load().llq_moe_gemm12(x_sorted.data_ptr(), expert_offsets.data_ptr(), sorted_slots.data_ptr(),
+                                tw.data_ptr(), n, E, H, inter, qw1.data_ptr(), sw1.data_ptr(), qw2.data_ptr(),
+                                sw2.data_ptr(), bits, _group_of(qw1, sw1, bits), h.data_ptr(), y.data_ptr(),
+                                counters.data_ptr(), _stream(x_sorted)), "moe_gemm12")
+    return y
+
+
+def gemm12_counters(n_rows: int, num_experts: int, device) -> torch.Tensor:
+    return torch.zeros(load().llq_moe_gemm12_counters(n_rows, num_experts), dtype=torch.int32, device=device)
+
+
 def moe_workspace(T: int, k: int, E: int, H: int, I: int, device) -> torch.Tensor:
     """A cached per-device workspace large enough for ``fused_moe_packed``."""
     need = load().llq_moe_workspace_size(T, k, E, H, I)

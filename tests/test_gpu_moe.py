@@ -232,3 +232,27 @@ def test_gemm2_one_hot_rows_read_back_the_dequantized_weights(impl, bits):
     ref = np.ascontiguousarray(ref.transpose(0, 2, 1)).reshape(n, H)
     got = to_np(y)
     assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), np.argwhere(got != ref)[:5]
+
+
+@pytest.mark.parametrize("T,bits", [(256, 4), (2048, 4), (300, 8)])
+def test_fused_gemm12_equals_the_two_launches(T, bits):
+    """GEMM1 and GEMM2 in one launch (GEMM2 work waits per token tile for its h rows) equal
+    the two separate launches bit for bit; the counters come back zeroed, so a second call
+    on the same buffer is right too."""
+    from llada_quant_b200 import ops
+    E, H, I, k = 16, 1024, 512, 2
+    r1, r2 = _quantize(E, H, I, bits)
+    x = synthetic_tokens(T, H).cuda()
+    tw, ids = random_routing(T, E, k, seed=T)
+    tw, ids = torch.from_numpy(tw).cuda(), torch.from_numpy(ids).cuda()
+    offsets, slots = ops.moe_align(ids, E)
+    xs = ops.moe_permute(x, slots, k)
+    code = _impl_or_skip("tcgen05", bits)
+    h = ops.moe_gemm1(xs, offsets, r1.q, r1.scale, bits, code)
+    y_ref = ops.moe_gemm2(h, offsets, slots, tw, r2.q, r2.scale, bits, code)
+    counters = ops.gemm12_counters(T * k, E, "cuda")
+    for _ in range(2):
+        y = ops._moe_gemm12_impl(xs, offsets, slots, tw, r1.q, r1.scale, r2.q, r2.scale, bits, counters)
+        torch.cuda.synchronize()
+        assert torch.equal(y, y_ref)
+        assert int(counters.abs().sum()) == 0
