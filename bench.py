@@ -608,10 +608,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                    "sample": f"one C3 layer call (256 tokens), {dt:.2f} s: "
                              + ("the reference's own dequantize_tensor (baseline/_ref) in torch + routed matmul"
                                 if kind == "reference" else "numpy port of the reference CPU path")}
-        # ours per step: router, align, permute, GEMM1, GEMM2, combine; at N > 1 over the
+        # ours per step: router, align, permute, GEMM1+GEMM2 (one launch in exact mode), combine; at N > 1 over the
         # window: router, dispatch, align, permute, GEMM1, GEMM2, combine; over NCCL: router,
         # rank grouping, pack, align, permute, GEMM1, GEMM2, combine, slot combine
-        launches_per_step = 6 if world == 1 else (7 if window is not None else 9)
+        fused_path = args.gemm in ("auto", "tcgen05")
+        launches_per_step = (5 if fused_path else 6) if world == 1 else (7 if window is not None else 9)
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
