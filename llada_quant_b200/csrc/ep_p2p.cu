@@ -117,6 +117,8 @@ struct EpWorkspace {
   size_t align_bytes;
   void* x_sorted;
   void* h_sorted;
+  int32_t* counters;  // the fused GEMMs' tile counters
+  int n_counters;
   size_t total;
 };
 
@@ -135,6 +137,8 @@ EpWorkspace carve_ep(void* base, int R, int cap, int E, int H, int I) {
   w.align_ws = take(w.align_bytes);
   w.x_sorted = take(static_cast<size_t>(n) * H * 2 + 4096);
   w.h_sorted = take(static_cast<size_t>(n) * I * 2 + 4096);
+  w.n_counters = gemm12_counter_slots(n, E);
+  w.counters = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * w.n_counters));
   w.total = off;
   return w;
 }
@@ -266,21 +270,27 @@ int llq_ep_experts(void* window, void* const* peers, int rank, int world, int ca
   m.R = world;
   m.epoch = epoch;
   m.timeout_ns = g_timeout_ns;
+  m.clear = ws.counters;
+  m.clear_n = ws.n_counters;
   rc = align_impl_masked(reinterpret_cast<const int32_t*>(mine + L.ids), n, E, ws.offsets, ws.sorted_slots,
                          ws.align_ws, ws.align_bytes, st, m);
   if (rc) return rc;
   rc = permute_impl(mine + L.rows, n, H, 1, ws.sorted_slots, ws.x_sorted, st, fast ? 1 : 0, ws.offsets + E);
   if (rc) return rc;
   if (rows_hint < 0) rows_hint = n;
-  rc = gemm1_tc(ws.x_sorted, ws.offsets, n, E, H, I, qw1, sw1, bits, group_size, ws.h_sorted, fast, st,
-                rows_hint);
-  if (rc) return rc;
   EpScatter sc{};
   sc.peers = reinterpret_cast<char* const*>(peers);
   sc.L = L;
   sc.me = rank;
   sc.epoch = epoch;
   sc.done = ep_done(mine, L, 1);
+  if (!fast)  // GEMM1 and GEMM2 in one launch; GEMM2 rows go straight to the source ranks
+    return gemm12_fused_tc(ws.x_sorted, ws.offsets, ws.sorted_slots, reinterpret_cast<const float*>(mine + L.wts), n,
+                           E, H, I, qw1, sw1, qw2, sw2, bits, group_size, ws.h_sorted, nullptr, ws.counters, st,
+                           rows_hint, &sc);
+  rc = gemm1_tc(ws.x_sorted, ws.offsets, n, E, H, I, qw1, sw1, bits, group_size, ws.h_sorted, fast, st,
+                rows_hint);
+  if (rc) return rc;
   return gemm2_tc(ws.h_sorted, ws.offsets, ws.sorted_slots, reinterpret_cast<const float*>(mine + L.wts), n, E,
                   H, I, qw2, sw2, bits, group_size, nullptr, fast, st, rows_hint, &sc);
 }

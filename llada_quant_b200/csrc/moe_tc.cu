@@ -847,7 +847,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     }
   }
 
-  if (!GEMM1 && args.ep_on && warp >= FIRST_EPI) __threadfence_system();  // rows stored to peers
+  if ((!GEMM1 || args.fused) && args.ep_on && warp >= FIRST_EPI) __threadfence_system();  // rows stored to peers
   tc_fence_before();
   __syncthreads();
   pdl_trigger();
@@ -865,7 +865,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }
-  if (!GEMM1 && args.ep_on && threadIdx.x == 0) {
+  if ((!GEMM1 || args.fused) && args.ep_on && threadIdx.x == 0) {
     // last CTA out tells every source rank that its rows are back
     if (atomicAdd(args.ep.done, 1u) == gridDim.x - 1) {
       __threadfence_system();
@@ -997,7 +997,7 @@ template <int BITS, int NTM>
 int launch_fused(const void* x_sorted, void* h_sorted, int64_t n_rows, const int32_t* offsets, int E, int H, int I,
                  const int8_t* qw1, const float* sw1, const int8_t* qw2, const float* sw2, int group_size,
                  const int32_t* sorted_slots, const float* topk_w, void* y_slots, int* tile_done,
-                 int tile_done_n, cudaStream_t st) {
+                 int tile_done_n, cudaStream_t st, const EpScatter* ep) {
   if (n_rows <= 0) return LLQ_OK;
   CUtensorMap tw[2], tb[2][4];
   int rc = phase_maps<BITS, NTM>(x_sorted, n_rows, H, E, 2 * I, qw1, &tw[0], tb[0]);
@@ -1018,7 +1018,8 @@ int launch_fused(const void* x_sorted, void* h_sorted, int64_t n_rows, const int
   a.tile_done = tile_done;
   a.tile_done_n = tile_done_n;
   a.debug = debug_flags();
-  a.ep_on = 0;
+  a.ep_on = ep != nullptr;  // GEMM2 rows go to the source ranks' windows
+  if (ep != nullptr) a.ep = *ep;
   return launch_kernel<true, BITS, false, NTM>(tw, tb, a, st);
 }
 
@@ -1128,20 +1129,21 @@ int gemm12_counter_slots(int64_t n_rows, int E) { return static_cast<int>(n_rows
 int gemm12_fused_tc(const void* x_sorted, const int32_t* offsets, const int32_t* sorted_slots, const float* topk_w,
                     int64_t n_rows, int E, int H, int I, const int8_t* qw1, const float* sw1, const int8_t* qw2,
                     const float* sw2, int bits, int group_size, void* h_sorted, void* y_slots, int* tile_done,
-                    cudaStream_t st) {
+                    cudaStream_t st, int64_t rows_hint, const EpScatter* ep) {
   if (!tc_supported(E, I, H, bits, group_size, true) || !tc_supported(E, H, I, bits, group_size, false))
     return fail(LLQ_EUNSUPPORTED, "tcgen05 expert GEMMs: unsupported shape");
   const int tile_done_n = gemm12_counter_slots(n_rows, E) - 1;
-  const bool wide = n_rows > static_cast<int64_t>(E) * 96;
+  if (rows_hint < 0) rows_hint = n_rows;
+  const bool wide = rows_hint > static_cast<int64_t>(E) * 96;
   if (bits == 4)
     return wide ? launch_fused<4, 128>(x_sorted, h_sorted, n_rows, offsets, E, H, I, qw1, sw1, qw2, sw2, group_size,
-                                       sorted_slots, topk_w, y_slots, tile_done, tile_done_n, st)
+                                       sorted_slots, topk_w, y_slots, tile_done, tile_done_n, st, ep)
                 : launch_fused<4, 64>(x_sorted, h_sorted, n_rows, offsets, E, H, I, qw1, sw1, qw2, sw2, group_size,
-                                      sorted_slots, topk_w, y_slots, tile_done, tile_done_n, st);
+                                      sorted_slots, topk_w, y_slots, tile_done, tile_done_n, st, ep);
   return wide ? launch_fused<8, 128>(x_sorted, h_sorted, n_rows, offsets, E, H, I, qw1, sw1, qw2, sw2, group_size,
-                                     sorted_slots, topk_w, y_slots, tile_done, tile_done_n, st)
+                                     sorted_slots, topk_w, y_slots, tile_done, tile_done_n, st, ep)
               : launch_fused<8, 64>(x_sorted, h_sorted, n_rows, offsets, E, H, I, qw1, sw1, qw2, sw2, group_size,
-                                    sorted_slots, topk_w, y_slots, tile_done, tile_done_n, st);
+                                    sorted_slots, topk_w, y_slots, tile_done, tile_done_n, st, ep);
 }
 
 }  // namespace llq
