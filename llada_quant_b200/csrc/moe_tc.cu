@@ -131,8 +131,6 @@ struct TcArgs {
   int* tile_done;  // fused: per token tile, GEMM1 epilogue warps finished; [tile_done_n] then a CTA counter
   int tile_done_n;
   int E;
-  int debug;       // development switch: 1 = no dequant math, 2 = no MMA, 4 = no TMEM stores,
-                   // 8 = no token-tile loads (results are wrong)
   int dense_rows;  // offsets == nullptr: one expert of this many rows, identity slots, weight 1
   int ksplit;      // K slices per output tile (> 1: exact GEMM2 only, fp32 partials to `partial`)
   float* partial;  // [ksplit][rows][n_out] when ksplit > 1
@@ -563,16 +561,14 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           const int s = it % S;
           if (!mbar_wait_sleep(&wfree[s], ((it / S) & 1) ^ 1, abort_flag, 0x110 + s)) { ok = false; break; }
           if (!mbar_wait_sleep(&mdone[s], ((it / S) & 1) ^ 1, abort_flag, 0x118 + s)) { ok = false; break; }
-          mbar_expect_tx(&full[s], C::W_STAGE_BYTES + ((args.debug & 8) ? 0 : 2 * box * 128));
+          mbar_expect_tx(&full[s], C::W_STAGE_BYTES + 2 * box * 128);
           LLQ_TRACE_AT(0, it);
           uint8_t* wdst = sw + s * C::W_STAGE_BYTES;
           tma_load_2d(wdst, tw, kc * C::W_ROW_BYTES, w0, &full[s]);
           tma_load_2d(wdst + C::W_TILE_BYTES, tw, kc * C::W_ROW_BYTES, w1, &full[s]);
           uint8_t* bdst = sb + s * C::B_STAGE_BYTES;
-          if (!(args.debug & 8)) {
-            tma_load_2d(bdst, tb, kc * KC, item.row0, &full[s]);
-            tma_load_2d(bdst + box * 128, tb, kc * KC + 64, item.row0, &full[s]);
-          }
+          tma_load_2d(bdst, tb, kc * KC, item.row0, &full[s]);
+          tma_load_2d(bdst + box * 128, tb, kc * KC + 64, item.row0, &full[s]);
           ++issued;
         }
       }
@@ -631,7 +627,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
             const int j = jj * SPLIT + par;
             const uint64_t bdesc = bdesc0 + (j >> 2) * half_step + (j & 3) * 2;
             const uint32_t acc = jj > 0 ? 1u : first;
-            if (!(args.debug & 2)) tc_mma(d, a_stage + j * 8, bdesc, idesc, acc);
+            tc_mma(d, a_stage + j * 8, bdesc, idesc, acc);
 #ifdef LLQ_TRACE
             if (tile == 0 && it >= 16 && it < 24) LLQ_TRACE_AT(7, (it - 16) * 8 + jj);
 #endif
@@ -659,6 +655,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
       const int sbuf = ii & 1;
       if (!mbar_wait(&sc_full[sbuf], (ii >> 1) & 1, abort_flag, 0x300)) break;
       const float* srow = ssc + sbuf * (2 * ROWS * MAX_G) + wg * (ROWS * MAX_G) + r * P.groups;
+      const int spg = P.group / KC;  // K steps per scale group (0: one scale per row)
       int kbeg, kper;
       k_range(item, kbeg, kper);
       for (int kc = kbeg; kc < kbeg + kper; ++kc, ++it) {
@@ -677,7 +674,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           const int pc = BITS == 4 ? (c ^ ((r >> 1) & 3)) : (c ^ (r & 7));  // 64/128-byte swizzle
           v[ci] = *reinterpret_cast<const uint4*>(wt + pc * 16);
         }
-        const float sc = FAST ? 0.f : srow[P.group > 0 ? (kc * KC) / P.group : 0];
+        const float sc = FAST ? 0.f : srow[spg == 1 ? kc : spg == 0 ? 0 : kc / spg];
         __syncwarp();
         if (lane == 0) mbar_arrive(&wfree[s]);
         // the TMEM A stage is free once the MMAs of step it - AS completed
@@ -691,13 +688,9 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
 #pragma unroll
           for (int ci = 0; ci < MYC; ++ci) {
             uint32_t o[16];
-            if (args.debug & 1) {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) o[i] = (i & 1) ? v[ci].y : v[ci].x;
-            } else if (FAST) codes_int4(v[ci], o);
+            if (FAST) codes_int4(v[ci], o);
             else dequant_int4_exact(v[ci], sc, o);
-            if (!(args.debug & 4)) tc_st16(a_stage + (c_lo + ci) * 16, o);
-            else asm volatile("" ::"r"(o[0]), "r"(o[5]), "r"(o[10]), "r"(o[15]));
+            tc_st16(a_stage + (c_lo + ci) * 16, o);
           }
         } else {
 #pragma unroll
@@ -940,14 +933,6 @@ inline TcPhase make_phase(bool gemm1, const float* scale, void* out, int K, int 
   return P;
 }
 
-inline int debug_flags() {
-  static const int flags = [] {
-    const char* e = getenv("LLQ_TC_DEBUG");
-    return e ? atoi(e) : 0;
-  }();
-  return flags;
-}
-
 template <bool GEMM1, int BITS, bool FAST, int NTM>
 int launch_kernel(const CUtensorMap (&tw)[2], const CUtensorMap (&tb)[2][4], const TcArgs& a, cudaStream_t st) {
   using C = Cfg<GEMM1, BITS, FAST, NTM>;
@@ -985,7 +970,6 @@ int launch_tc(const void* act, int64_t n_rows, const int32_t* offsets, int E, in
   a.ph[1] = a.ph[0];
   a.fused = 0;
   a.tile_done = nullptr;
-  a.debug = debug_flags();
   a.ep_on = ep != nullptr;
   if (ep != nullptr) a.ep = *ep;
   return launch_kernel<GEMM1, BITS, FAST, NTM>(tw, tb, a, st);
@@ -1017,7 +1001,6 @@ int launch_fused(const void* x_sorted, void* h_sorted, int64_t n_rows, const int
   a.fused = 1;
   a.tile_done = tile_done;
   a.tile_done_n = tile_done_n;
-  a.debug = debug_flags();
   a.ep_on = ep != nullptr;  // GEMM2 rows go to the source ranks' windows
   if (ep != nullptr) a.ep = *ep;
   return launch_kernel<true, BITS, false, NTM>(tw, tb, a, st);
