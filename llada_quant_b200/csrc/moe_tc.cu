@@ -518,7 +518,8 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
   if (warp == 0) {
     // ------------------------------------------------------------- producer
     if (lane == 0) {
-      int it = 0, issued = 0;
+      int it = 0, issued = 0, rs = 0;
+      uint32_t rph = 0;  // ring slot and phase of step it
       bool ok = true;
       for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
         const Item item = item_at(u);
@@ -558,9 +559,9 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         int kbeg, kper;
         k_range(item, kbeg, kper);
         for (int kc = kbeg; kc < kbeg + kper; ++kc, ++it) {
-          const int s = it % S;
-          if (!mbar_wait_sleep(&wfree[s], ((it / S) & 1) ^ 1, abort_flag, 0x110 + s)) { ok = false; break; }
-          if (!mbar_wait_sleep(&mdone[s], ((it / S) & 1) ^ 1, abort_flag, 0x118 + s)) { ok = false; break; }
+          const int s = rs;
+          if (!mbar_wait_sleep(&wfree[s], rph ^ 1, abort_flag, 0x110 + s)) { ok = false; break; }
+          if (!mbar_wait_sleep(&mdone[s], rph ^ 1, abort_flag, 0x118 + s)) { ok = false; break; }
           mbar_expect_tx(&full[s], C::W_STAGE_BYTES + 2 * box * 128);
           LLQ_TRACE_AT(0, it);
           uint8_t* wdst = sw + s * C::W_STAGE_BYTES;
@@ -570,6 +571,10 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           tma_load_2d(bdst, tb, kc * KC, item.row0, &full[s]);
           tma_load_2d(bdst + box * 128, tb, kc * KC + 64, item.row0, &full[s]);
           ++issued;
+          if (++rs == S) {
+            rs = 0;
+            rph ^= 1;
+          }
         }
       }
       // never leave copies in flight into this CTA's shared memory
@@ -585,7 +590,8 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     const int par = (warp - 1) >> 1;      // K-slice parity (SPLIT == 2)
     if (lane == 0) {
       const uint32_t a_base = tmem + C::ACC_COLS;
-      int it = 0;
+      int it = 0, rs = 0, ra = 0;
+      uint32_t rph = 0, raph = 0;  // ring slot / phase and TMEM A stage / phase of step it
       bool ok = true;
       for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
         const Item item = item_at(u);
@@ -602,7 +608,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         k_range(item, kbeg, kper);
         const int kend = kbeg + kper;
         for (int kc = kbeg; kc < kend; ++kc, ++it) {
-          const int s = it % S, sa = it % AS;
+          const int s = rs, sa = ra;
           const uint32_t acc_base = tmem + (C::ACC_BUFS == 2 ? (ii & 1) * C::ACC_BUF_COLS : 0);
           uint32_t d0 = acc_base + par * NTM, d1 = acc_base + (SPLIT + par) * NTM;
           if (FAST) {
@@ -611,9 +617,9 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
             d0 = tmem + pb * 2 * NTM;
             d1 = d0 + NTM;
           }
-          if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, 0x220 + s)) { ok = false; break; }
+          if (!mbar_wait(&full[s], rph, abort_flag, 0x220 + s)) { ok = false; break; }
           if (tile == 0) LLQ_TRACE_AT(4, it);
-          if (!mbar_wait(&a_full[tile * AS + sa], (it / AS) & 1, abort_flag, 0x230 + sa)) { ok = false; break; }
+          if (!mbar_wait(&a_full[tile * AS + sa], raph, abort_flag, 0x230 + sa)) { ok = false; break; }
           if (tile == 0) LLQ_TRACE_AT(5, it);
           tc_fence_after();
           // descriptors advance by plain adds on the 16-byte-unit start address
@@ -635,6 +641,14 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           tc_commit(&mdone[s]);
           if (tile == 0) LLQ_TRACE_AT(6, it);
           if (!FAST && kc == kend - 1) tc_commit(&acc_full[C::ACC_BUFS == 2 ? (ii & 1) : 0]);
+          if (++rs == S) {
+            rs = 0;
+            rph ^= 1;
+          }
+          if (++ra == AS) {
+            ra = 0;
+            raph ^= 1;
+          }
         }
       }
     }
@@ -647,7 +661,8 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     const int q = warp & 3;                 // TMEM lane quarter
     const int r = q * 32 + lane;            // row within the tile
     const uint32_t a_row = tmem + C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16) + wg * (KC / 2);
-    int it = 0;
+    int it = 0, rs = 0, ps = S - AS, ra = 0;  // ring slots of steps it and it - AS, TMEM A stage of it
+    uint32_t rph = 0, pph = 1;                // their phases
     bool ok = true;
     for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
       const Item item = item_at(u);
@@ -659,8 +674,9 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
       int kbeg, kper;
       k_range(item, kbeg, kper);
       for (int kc = kbeg; kc < kbeg + kper; ++kc, ++it) {
-        const int s = it % S, sa = it % AS;
-        if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, 0x310 + s)) { ok = false; break; }
+        const int s = rs, sa = ra;
+        const float sc = FAST ? 0.f : srow[spg == 1 ? kc : spg == 0 ? 0 : kc / spg];
+        if (!mbar_wait(&full[s], rph, abort_flag, 0x310 + s)) { ok = false; break; }
         if (warp == FIRST_DQ) LLQ_TRACE_AT(1, it);
         const uint8_t* wt = sw + s * C::W_STAGE_BYTES + wg * C::W_TILE_BYTES + r * C::W_ROW_BYTES;
         const uint32_t a_stage = a_row + sa * C::A_STAGE_COLS;
@@ -674,14 +690,10 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           const int pc = BITS == 4 ? (c ^ ((r >> 1) & 3)) : (c ^ (r & 7));  // 64/128-byte swizzle
           v[ci] = *reinterpret_cast<const uint4*>(wt + pc * 16);
         }
-        const float sc = FAST ? 0.f : srow[spg == 1 ? kc : spg == 0 ? 0 : kc / spg];
         __syncwarp();
         if (lane == 0) mbar_arrive(&wfree[s]);
         // the TMEM A stage is free once the MMAs of step it - AS completed
-        if (it >= AS) {
-          const int pit = it - AS;
-          if (!mbar_wait(&mdone[pit % S], (pit / S) & 1, abort_flag, 0x320 + sa)) { ok = false; break; }
-        }
+        if (it >= AS && !mbar_wait(&mdone[ps], pph, abort_flag, 0x320 + sa)) { ok = false; break; }
         if (warp == FIRST_DQ) LLQ_TRACE_AT(2, it);
         tc_fence_after();
         if (BITS == 4) {
@@ -708,6 +720,15 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           mbar_arrive(&a_full[wg * AS + sa]);
           if (warp == FIRST_DQ) LLQ_TRACE_AT(3, it);
         }
+        if (++rs == S) {
+          rs = 0;
+          rph ^= 1;
+        }
+        if (++ps == S) {
+          ps = 0;
+          pph ^= 1;
+        }
+        if (++ra == AS) ra = 0;
       }
       __syncwarp();
       if (ok && lane == 0) mbar_arrive(&sc_empty[sbuf]);
