@@ -268,7 +268,7 @@ int quantize_impl(const void* w, int w_dtype, int64_t rows, int64_t K, int bits,
                   "int4 packing needs an even group_size so groups stay byte-aligned, got %d",
                   group_size);
   }
-  int seg_len, spr;
+  int seg_len = 0, spr = 0;
   int rc = segments(K, group_size, &seg_len, &spr);
   if (rc) return rc;
   switch (w_dtype) {
