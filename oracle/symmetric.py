@@ -75,9 +75,19 @@ def validate_int4_layout(shape, group_size: int) -> None:
         )
 
 
-def amax_scale(w_g: np.ndarray, bits: int) -> np.ndarray:
-    """``_amax_scale`` (symmetric.py:117-119): fp32 amax divided (not multiplied) by Qmax."""
+def amax_scale(w_g: np.ndarray, bits: int, reciprocal: bool = False) -> np.ndarray:
+    """``_amax_scale`` (symmetric.py:117-119): fp32 amax divided (not multiplied) by Qmax.
+
+    ``reciprocal=True`` gives what the same line computes when the reference runs
+    in CUDA torch: ATen's CUDA kernel divides a tensor by a Python scalar as a
+    multiplication by the float32 reciprocal, amax * float32(1/Qmax), which is
+    one ulp off the division for part of the groups.  The kernels follow the
+    division (CPU torch, the golden vectors); tests use this form only to explain
+    the differences from a CUDA-torch run of the reference.
+    """
     amax = np.abs(w_g).max(axis=-1, keepdims=True).astype(np.float32)
+    if reciprocal:
+        return (amax * np.float32(1.0 / qmax_for_bits(bits))).astype(np.float32)
     return (amax / np.float32(qmax_for_bits(bits))).astype(np.float32)
 
 
@@ -93,7 +103,7 @@ def group_sse_terms(wf: np.ndarray, safe: np.ndarray, bits: int) -> np.ndarray:
 
 
 def search_group_scale(w_g: np.ndarray, bits: int, grid: int = 24, max_shrink: float = 0.5,
-                       sum_dtype=np.float64, return_errors: bool = False):
+                       sum_dtype=np.float64, return_errors: bool = False, reciprocal: bool = False):
     """``search_group_scale`` (symmetric.py:122-204).
 
     ``ratio`` is a Python double, then rounded to float32 when it multiplies the
@@ -106,14 +116,15 @@ def search_group_scale(w_g: np.ndarray, bits: int, grid: int = 24, max_shrink: f
     rounded float32 terms in float64 by default, i.e. it picks the truly best
     candidate; the callers report how often that differs from the reference
     (only ever at near-ties).  Chunking (symmetric.py:164-180) does not change
-    the result and is not restated.
+    the result and is not restated.  ``reciprocal`` selects the CUDA-torch form of
+    the base scale (see ``amax_scale``).
     """
     if grid < 1:
         raise ValueError(f"grid must be >= 1, got {grid}")
     if not 0.0 <= max_shrink < 1.0:
         raise ValueError(f"max_shrink must lie in [0, 1), got {max_shrink}")
     wf = w_g.astype(np.float32)
-    base = amax_scale(w_g, bits)
+    base = amax_scale(w_g, bits, reciprocal)
     best_scale = base.copy()
     best_err = np.full(base.shape, np.inf, dtype=sum_dtype)
     errors = []
