@@ -83,6 +83,9 @@ def load_to_device(path: str, device, names: Optional[Iterable[str]] = None,
         out[n] = t
         dst_bytes[n] = t.view(-1).view(torch.uint8) if t.numel() else t
     stream = torch.cuda.Stream(device)
+    # the destinations come from the caching allocator on the current stream: a block
+    # freed there may still be read by queued kernels, so the copies start after them
+    stream.wait_stream(torch.cuda.current_stream(device))
     stage = [torch.empty(chunk_bytes, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
     done = [None, None]
     with open(path, "rb", buffering=0) as f, torch.cuda.stream(stream):

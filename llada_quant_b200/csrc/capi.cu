@@ -69,15 +69,6 @@ MoeWorkspace carve(void* base, int64_t T, int k, int E, int H, int I) {
   return w;
 }
 
-// LLQ_FUSED_GEMMS=0 runs GEMM1 and GEMM2 as two launches (development A/B switch)
-bool fused_gemms() {
-  static const bool on = [] {
-    const char* e = getenv("LLQ_FUSED_GEMMS");
-    return e == nullptr || atoi(e) != 0;
-  }();
-  return on;
-}
-
 int pick_impl(int impl, int E, int N_out, int K, int bits, int group_size, bool gemm1) {
   if (impl == LLQ_GEMM_SIMT) return LLQ_GEMM_SIMT;
   const bool tc = tc_supported(E, N_out, K, bits, group_size, gemm1);
@@ -265,7 +256,7 @@ int llq_fused_moe_packed(const void* x, const int8_t* qw1, const float* sw1, con
   }
   rc = permute_impl(x, T, H, k, ws.sorted_slots, ws.x_sorted, st, 0);
   if (rc) return rc;
-  if (fused_gemms() && pick_impl(impl, E, I, H, bits, group_size, true) == LLQ_GEMM_TCGEN05 &&
+  if (pick_impl(impl, E, I, H, bits, group_size, true) == LLQ_GEMM_TCGEN05 &&
       pick_impl(impl, E, H, I, bits, group_size, false) == LLQ_GEMM_TCGEN05) {
     rc = gemm12_fused_tc(ws.x_sorted, ws.offsets, ws.sorted_slots, topk_w, n, E, H, I, qw1, sw1, qw2, sw2, bits,
                          group_size, ws.h_sorted, ws.y_slots, ws.tile_done, st);

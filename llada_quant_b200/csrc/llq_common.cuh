@@ -8,6 +8,7 @@
 #include <stdio.h>
 #include <string>
 #include <cstdlib>
+#include <atomic>
 #include <utility>
 
 #include "../../include/llada_quant.h"
@@ -28,15 +29,32 @@ inline int check_launch(const char* what) {
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// SM count of the current device (cached per device ordinal)
 inline int num_sms() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
+  constexpr int kMaxDev = 64;
+  static int cache[kMaxDev] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) dev = 0;
+  if (dev >= kMaxDev) {
+    int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
+    return n > 0 ? n : 148;
   }
-  return n;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+// true once per (flag set, device): callers use it to set per-device kernel attributes
+// (setting a function attribute twice is harmless, so a race only repeats it)
+inline bool first_use_on_device(std::atomic<uint64_t>& seen_mask) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return true;
+  const uint64_t bit = 1ull << dev;
+  return (seen_mask.fetch_or(bit) & bit) == 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -44,18 +62,9 @@ inline int num_sms() {
 // next one is scheduled while the previous one drains; each waits for its
 // predecessor's results (griddepcontrol.wait, a no-op without the attribute)
 // before reading them and releases its dependents once its work is issued.
-// LLQ_PDL=0 turns the attribute off.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-
-inline bool pdl_enabled() {
-  static const bool on = [] {
-    const char* e = getenv("LLQ_PDL");
-    return e == nullptr || atoi(e) != 0;
-  }();
-  return on;
-}
 
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
@@ -67,7 +76,7 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);

@@ -33,6 +33,8 @@ int gemm2_tc(const void*, const int32_t*, const int32_t*, const float*, int64_t,
              const int8_t*, const float*, int, int, void*, bool, cudaStream_t, int64_t rows_hint = -1,
              const EpScatter* ep = nullptr);
 bool tc_supported(int E, int N_out, int K, int bits, int group_size, bool gemm1);
+// implementation an LLQ_GEMM_* request resolves to for one expert GEMM, or -1
+int pick_impl(int impl, int E, int N_out, int K, int bits, int group_size, bool gemm1);
 
 int dense_ksplit(int64_t M, int K, int N);
 int gemm12_counter_slots(int64_t n_rows, int E);

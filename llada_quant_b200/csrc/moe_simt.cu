@@ -119,11 +119,9 @@ int launch_simt(const void* a, const int32_t* offsets, int E, int N_out, int K, 
   if (rc) return rc;
   const size_t smem = static_cast<size_t>(kTileRows) * K * 2;
   if (smem > 200 * 1024) return fail(LLQ_EUNSUPPORTED, "K=%d too large for the SIMT GEMM", K);
-  static bool attr = false;
-  if (!attr) {
+  static std::atomic<uint64_t> attr{0};
+  if (first_use_on_device(attr))
     cudaFuncSetAttribute(moe_gemm_simt_kernel<GEMM1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr = true;
-  }
   dim3 grid((N_out + kTileN - 1) / kTileN, E);
   moe_gemm_simt_kernel<GEMM1><<<grid, kThreads, smem, st>>>(
       static_cast<const __nv_bfloat16*>(a), offsets, N_out, K, inter, q, scale, bits, group,

@@ -50,21 +50,6 @@ constexpr int MAX_G = 16;  // scale groups per row (K <= 2048 at group 128)
 constexpr int MAX_E = 256;
 constexpr long long kTimeoutCycles = 4000000000LL;
 
-// Development timeline (built only with -DLLQ_TRACE): clock64 of each role's
-// progress through the first 64 K-steps of CTA 0.
-#ifdef LLQ_TRACE
-__device__ long long g_tc_trace[8][64];
-#define LLQ_TRACE_AT(role, step)                                              \
-  do {                                                                        \
-    if (blockIdx.x == 0 && (threadIdx.x & 31) == 0 && (step) < 64)           \
-      g_tc_trace[(role)][(step)] = clock64();                                 \
-  } while (0)
-#else
-#define LLQ_TRACE_AT(role, step) \
-  do {                           \
-  } while (0)
-#endif
-
 template <bool GEMM1, int BITS, bool FAST, int NTM>
 struct Cfg {
   static constexpr int W_ROW_BYTES = KC * BITS / 8;
@@ -231,20 +216,37 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-__device__ __forceinline__ void tc_mma(uint32_t d, uint32_t a, uint64_t bdesc, uint32_t idesc,
-                                       uint32_t accumulate) {
+// 1 in exactly one lane of the (converged) warp, 0 in the others
+__device__ __forceinline__ uint32_t elect_one() {
+  uint32_t e;
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .pred p;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(e));
+  return e;
+}
+
+// issued by the lanes with `issue` != 0 (one per warp)
+__device__ __forceinline__ void tc_mma(uint32_t d, uint32_t a, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate, uint32_t issue) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
-      "r"(a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      "setp.ne.b32 q, %5, 0;\n\t"
+      "@q tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(issue)
       : "memory");
 }
 
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
+__device__ __forceinline__ void tc_commit(uint64_t* bar, uint32_t issue) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\t"
+      "setp.ne.b32 q, %1, 0;\n\t"
+      "@q tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          smem_u32(bar)),
+      "r"(issue)
+      : "memory");
 }
 
 __device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&v)[16]) {
@@ -563,7 +565,6 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           if (!mbar_wait_sleep(&wfree[s], rph ^ 1, abort_flag, 0x110 + s)) { ok = false; break; }
           if (!mbar_wait_sleep(&mdone[s], rph ^ 1, abort_flag, 0x118 + s)) { ok = false; break; }
           mbar_expect_tx(&full[s], C::W_STAGE_BYTES + 2 * box * 128);
-          LLQ_TRACE_AT(0, it);
           uint8_t* wdst = sw + s * C::W_STAGE_BYTES;
           tma_load_2d(wdst, tw, kc * C::W_ROW_BYTES, w0, &full[s]);
           tma_load_2d(wdst + C::W_TILE_BYTES, tw, kc * C::W_ROW_BYTES, w1, &full[s]);
@@ -588,7 +589,10 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     // ------------------------------------------------------------- MMA issuers
     const int tile = (warp - 1) & 1;      // weight tile
     const int par = (warp - 1) >> 1;      // K-slice parity (SPLIT == 2)
-    if (lane == 0) {
+    // the whole warp runs the loop (its descriptor arithmetic stays warp-uniform);
+    // one elected lane issues the MMAs and the commits that track them
+    const uint32_t leader = elect_one();
+    {
       const uint32_t a_base = tmem + C::ACC_COLS;
       int it = 0, rs = 0, ra = 0;
       uint32_t rph = 0, raph = 0;  // ring slot / phase and TMEM A stage / phase of step it
@@ -618,9 +622,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
             d1 = d0 + NTM;
           }
           if (!mbar_wait(&full[s], rph, abort_flag, 0x220 + s)) { ok = false; break; }
-          if (tile == 0) LLQ_TRACE_AT(4, it);
           if (!mbar_wait(&a_full[tile * AS + sa], raph, abort_flag, 0x230 + sa)) { ok = false; break; }
-          if (tile == 0) LLQ_TRACE_AT(5, it);
           tc_fence_after();
           // descriptors advance by plain adds on the 16-byte-unit start address
           const uint64_t bdesc0 = make_sdesc(smem_u32(sb + s * C::B_STAGE_BYTES));
@@ -633,14 +635,10 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
             const int j = jj * SPLIT + par;
             const uint64_t bdesc = bdesc0 + (j >> 2) * half_step + (j & 3) * 2;
             const uint32_t acc = jj > 0 ? 1u : first;
-            tc_mma(d, a_stage + j * 8, bdesc, idesc, acc);
-#ifdef LLQ_TRACE
-            if (tile == 0 && it >= 16 && it < 24) LLQ_TRACE_AT(7, (it - 16) * 8 + jj);
-#endif
+            tc_mma(d, a_stage + j * 8, bdesc, idesc, acc, leader);
           }
-          tc_commit(&mdone[s]);
-          if (tile == 0) LLQ_TRACE_AT(6, it);
-          if (!FAST && kc == kend - 1) tc_commit(&acc_full[C::ACC_BUFS == 2 ? (ii & 1) : 0]);
+          tc_commit(&mdone[s], leader);
+          if (!FAST && kc == kend - 1) tc_commit(&acc_full[C::ACC_BUFS == 2 ? (ii & 1) : 0], leader);
           if (++rs == S) {
             rs = 0;
             rph ^= 1;
@@ -677,7 +675,6 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         const int s = rs, sa = ra;
         const float sc = FAST ? 0.f : srow[spg == 1 ? kc : spg == 0 ? 0 : kc / spg];
         if (!mbar_wait(&full[s], rph, abort_flag, 0x310 + s)) { ok = false; break; }
-        if (warp == FIRST_DQ) LLQ_TRACE_AT(1, it);
         const uint8_t* wt = sw + s * C::W_STAGE_BYTES + wg * C::W_TILE_BYTES + r * C::W_ROW_BYTES;
         const uint32_t a_stage = a_row + sa * C::A_STAGE_COLS;
         // this row's packed bytes into registers, then hand the weight slot back
@@ -694,7 +691,6 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         if (lane == 0) mbar_arrive(&wfree[s]);
         // the TMEM A stage is free once the MMAs of step it - AS completed
         if (it >= AS && !mbar_wait(&mdone[ps], pph, abort_flag, 0x320 + sa)) { ok = false; break; }
-        if (warp == FIRST_DQ) LLQ_TRACE_AT(2, it);
         tc_fence_after();
         if (BITS == 4) {
 #pragma unroll
@@ -716,10 +712,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&a_full[wg * AS + sa]);
-          if (warp == FIRST_DQ) LLQ_TRACE_AT(3, it);
-        }
+        if (lane == 0) mbar_arrive(&a_full[wg * AS + sa]);
         if (++rs == S) {
           rs = 0;
           rph ^= 1;
@@ -957,12 +950,10 @@ inline TcPhase make_phase(bool gemm1, const float* scale, void* out, int K, int 
 template <bool GEMM1, int BITS, bool FAST, int NTM>
 int launch_kernel(const CUtensorMap (&tw)[2], const CUtensorMap (&tb)[2][4], const TcArgs& a, cudaStream_t st) {
   using C = Cfg<GEMM1, BITS, FAST, NTM>;
-  static bool attr = false;
-  if (!attr) {
+  static std::atomic<uint64_t> attr{0};
+  if (first_use_on_device(attr))
     cudaFuncSetAttribute(moe_gemm_tc_kernel<GEMM1, BITS, FAST, NTM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(C::SMEM_BYTES));
-    attr = true;
-  }
   launch_pdl(moe_gemm_tc_kernel<GEMM1, BITS, FAST, NTM>, dim3(num_sms()), dim3(C::THREADS), C::SMEM_BYTES, st,
              tw[0], tb[0][0], tb[0][1], tb[0][2], tb[0][3], tw[1], tb[1][0], tb[1][1], tb[1][2], tb[1][3], a);
   return check_launch("moe_gemm_tc_kernel");
@@ -1152,11 +1143,6 @@ int gemm12_fused_tc(const void* x_sorted, const int32_t* offsets, const int32_t*
 
 }  // namespace llq
 
-#ifdef LLQ_TRACE
-extern "C" int llq_trace_read(long long* host) {
-  return cudaMemcpyFromSymbol(host, llq::g_tc_trace, sizeof(long long) * 8 * 64) == cudaSuccess ? 0 : 3;
-}
-#endif
 
 namespace llq {
 

@@ -92,6 +92,13 @@ int llq_fused_moe_packed_noalloc(const void* x, const int8_t* qw1, const float* 
                 kNoAllocMaxExperts);
   if (align_workspace_size(T, k, E) > kAlignBytes)
     return fail(LLQ_EINVAL, "llq_fused_moe_packed_noalloc: alignment scratch too small");
+  // the fast GEMM1 expects its token rows in the K-interleaved order its code
+  // expansion produces, exactly as in llq_fused_moe_packed
+  const bool fast = impl == LLQ_GEMM_TCGEN05_FAST;
+  if (fast && (pick_impl(impl, E, I, H, bits, group_size, true) < 0 ||
+               pick_impl(impl, E, H, I, bits, group_size, false) < 0))
+    return fail(LLQ_EUNSUPPORTED, "LLQ_GEMM_TCGEN05_FAST does not cover this shape (INT4, K <= 2048, "
+                                  "I %% 128 == 0, H %% 256 == 0, group %% 128 == 0)");
   if (T == 0) return LLQ_OK;
   unsigned char* base = nullptr;
   int rc = scratch_on_current_device(&base);
@@ -104,7 +111,7 @@ int llq_fused_moe_packed_noalloc(const void* x, const int8_t* qw1, const float* 
   cudaStream_t st = as_stream(stream);
   rc = align_impl(topk_ids, T, k, E, offsets, slots, align_ws, kAlignBytes, st);
   if (rc) return rc;
-  rc = permute_impl(x, T, H, k, slots, acts, st, 0);
+  rc = permute_impl(x, T, H, k, slots, acts, st, fast ? 1 : 0);
   if (rc) return rc;
   rc = llq_moe_gemm1(acts, offsets, rows, E, H, I, qw1, sw1, bits, group_size, inter, impl, stream);
   if (rc) return rc;

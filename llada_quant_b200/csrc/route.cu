@@ -633,11 +633,9 @@ int launch_route(const void* x, const void* gate_w, int64_t T, int H, int E, int
                  int renormalize, void* logits, float* topk_w, int32_t* topk_ids, cudaStream_t st) {
   const size_t smem = static_cast<size_t>(TOK) * H * 4 + static_cast<size_t>(TOK) * E * 4;
   if (smem > 200 * 1024) return fail(LLQ_EUNSUPPORTED, "hidden size %d too large for the router", H);
-  static bool attr_set = false;
-  if (!attr_set) {
+  static std::atomic<uint64_t> attr{0};
+  if (first_use_on_device(attr))
     cudaFuncSetAttribute(route_kernel<TOK>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr_set = true;
-  }
   const unsigned blocks = static_cast<unsigned>((T + TOK - 1) / TOK);
   route_kernel<TOK><<<blocks, kRouteThreads, smem, st>>>(static_cast<const __nv_bfloat16*>(x),
                                                          static_cast<const __nv_bfloat16*>(gate_w), T, H, E, k,
@@ -653,11 +651,7 @@ int route_impl(const void* x, const void* gate_w, int64_t T, int H, int E, int k
   if (k < 1 || k > E || k > 32) return fail(LLQ_EINVAL, "top_k must be in [1, min(E, 32)], got %d", k);
   if (H % 8 != 0) return fail(LLQ_EUNSUPPORTED, "hidden size must be a multiple of 8, got %d", H);
   // enough blocks to cover the SMs at decode sizes, more tokens per weight pass at prefill sizes
-  static const int forced = [] {
-    const char* e = getenv("LLQ_ROUTE_TOK");
-    return e ? atoi(e) : 0;
-  }();
-  if (forced == 0 && E % 8 == 0 && E <= 64 && H % (kRmWarps * 32) == 0) {
+  if (E % 8 == 0 && E <= 64 && H % (kRmWarps * 32) == 0) {
     const size_t smem = static_cast<size_t>(kRmWarps) * 16 * E * 4;
     const unsigned blocks = static_cast<unsigned>((T + 15) / 16);
     auto* xp = static_cast<const __nv_bfloat16*>(x);
@@ -665,11 +659,9 @@ int route_impl(const void* x, const void* gate_w, int64_t T, int H, int E, int k
     auto* lp = static_cast<__nv_bfloat16*>(logits);
 #define LLQ_ROUTE_MMA(NT)                                                                                  \
   case NT: {                                                                                               \
-    static bool attr = false;                                                                              \
-    if (!attr) {                                                                                           \
+    static std::atomic<uint64_t> attr{0};                                                                  \
+    if (first_use_on_device(attr))                                                                         \
       cudaFuncSetAttribute(route_mma_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);  \
-      attr = true;                                                                                         \
-    }                                                                                                      \
     launch_pdl(route_mma_kernel<NT>, dim3(blocks), dim3(kRmWarps * 32), smem, st, xp, wp, T, H, k, bias,    \
                renormalize, lp, topk_w, topk_ids);                                                         \
     return check_launch("route_mma_kernel");                                                               \
@@ -689,7 +681,6 @@ int route_impl(const void* x, const void* gate_w, int64_t T, int H, int E, int k
   }
   const int sms = num_sms();
   int tok = T <= sms ? 1 : T <= 2 * sms ? 2 : T <= 8 * sms ? 4 : 8;
-  if (forced == 1 || forced == 2 || forced == 4 || forced == 8) tok = forced;
   if (static_cast<size_t>(tok) * H * 4 + static_cast<size_t>(tok) * E * 4 > 200 * 1024) tok = 1;
   switch (tok) {
     case 1: return launch_route<1>(x, gate_w, T, H, E, k, bias, renormalize, logits, topk_w, topk_ids, st);
