@@ -39,6 +39,24 @@
 #include "llq_common.cuh"
 #include "ep_window.cuh"
 
+#ifndef LLQ_X_NOMMA
+#define LLQ_X_NOMMA 0
+#endif
+#ifndef LLQ_X_NOTOK
+#define LLQ_X_NOTOK 0
+#endif
+#ifndef LLQ_X_NODQ
+#define LLQ_X_NODQ 0
+#endif
+#ifndef LLQ_X_SPLIT
+#define LLQ_X_SPLIT 1
+#endif
+#ifndef LLQ_X_DQW
+#define LLQ_X_DQW 8
+#endif
+#ifndef LLQ_X_EPW
+#define LLQ_X_EPW 8
+#endif
 namespace llq {
 
 namespace {
@@ -56,10 +74,15 @@ struct Cfg {
   static constexpr int W_TILE_BYTES = ROWS * W_ROW_BYTES;
   static constexpr int W_STAGE_BYTES = 2 * W_TILE_BYTES;
   static constexpr int B_STAGE_BYTES = NTM * KC * 2;
-  static constexpr int STAGE_BYTES = W_STAGE_BYTES + B_STAGE_BYTES;
   static constexpr int SCALE_BUF_BYTES = 2 * ROWS * MAX_G * 4;
-  static constexpr int STAGES_FIT = (220 * 1024 - 2 * SCALE_BUF_BYTES) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
+  // Two rings: packed weights, released as soon as the dequantizing warps have
+  // copied them to registers, and token tiles, released when the step's MMAs
+  // complete.  Weight slots thus turn over at the speed of HBM, independently
+  // of the MMA pipeline, and the weight ring takes what shared memory is left.
+  static constexpr int B_STAGES = B_STAGE_BYTES <= 16384 ? 4 : 3;
+  static constexpr int W_STAGES_FIT =
+      (220 * 1024 - 2 * SCALE_BUF_BYTES - B_STAGES * B_STAGE_BYTES) / W_STAGE_BYTES;
+  static constexpr int W_STAGES = W_STAGES_FIT > 8 ? 8 : W_STAGES_FIT;
   // Warp roles.  A warp issues one tcgen05.mma per ~55 cycles whatever N is,
   // while a 128 x N x 16 MMA with N <= 64 runs in 16-32 cycles, so small-N
   // tiles are fed by several issuing warps: one per weight tile, optionally
@@ -68,14 +91,15 @@ struct Cfg {
   // (measured on B200 at C3: splitting K across four issuers with 16 dequant
   // warps gained nothing over two issuers with 8 -- exact dequantization is
   // then ALU-bound -- so SPLIT stays 1; the code keeps both layouts correct)
-  static constexpr int SPLIT = 1;
+  static constexpr int SPLIT = LLQ_X_SPLIT;
   static constexpr int MMA_WARPS = 2 * SPLIT;
   // (measured at C3: 16 dequantizing warps with one epilogue warpgroup made
   // the exact GEMM1 11% slower than 8 + 8; the code supports both)
-  static constexpr int DQ_WARPS = 8;
-  static constexpr int EPI_WARPS = 8;  // token groups of one warpgroup each
+  static constexpr int DQ_WARPS = LLQ_X_DQW;
+  static constexpr int EPI_WARPS = LLQ_X_EPW;  // token groups of one warpgroup each
   static constexpr int DQ_PARTS = DQ_WARPS / 8;  // warpgroups per weight tile
-  static constexpr int FIRST_DQ = 1 + MMA_WARPS;
+  static constexpr int FIRST_MMA = 2;  // warp 0 loads weights and scales, warp 1 token tiles
+  static constexpr int FIRST_DQ = FIRST_MMA + MMA_WARPS;
   static constexpr int FIRST_EPI = FIRST_DQ + DQ_WARPS;
   static constexpr int THREADS = (FIRST_EPI + EPI_WARPS) * 32;
   // exact mode: the accumulators are double-buffered across items when they
@@ -89,8 +113,10 @@ struct Cfg {
   static constexpr int A_STAGES = A_STAGES_FIT > 4 ? 4 : A_STAGES_FIT;
   static constexpr int CHUNKS = W_ROW_BYTES / 16;
   static constexpr size_t SMEM_BYTES =
-      1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + 2 * SCALE_BUF_BYTES + 2048;
-  static_assert(STAGES >= 2 && A_STAGES >= 2, "pipeline too shallow");
+      1024 + static_cast<size_t>(W_STAGES) * W_STAGE_BYTES + static_cast<size_t>(B_STAGES) * B_STAGE_BYTES +
+      2 * SCALE_BUF_BYTES + 2048;
+  static_assert(W_STAGES >= 2 && B_STAGES >= 2 && A_STAGES >= 2, "pipeline too shallow");
+  static_assert(A_STAGES <= B_STAGES, "a TMEM A stage is released through the token ring");
   static_assert(!FAST || BITS == 4, "fast mode is INT4 only");
 };
 
@@ -310,10 +336,47 @@ __device__ __forceinline__ uint32_t scale_pair_to_bf16x2(uint32_t lo_bits, uint3
   return o;
 }
 
-// 16 packed bytes = 32 int4 values -> 16 bf16x2 words, natural K order
-__device__ __forceinline__ void dequant_int4_exact(uint4 v, float s, uint32_t (&out)[16]) {
-  const float s16 = s * 0.0625f;
+// (x & mask) ^ k in one LOP3
+__device__ __forceinline__ uint32_t and_xor(uint32_t x, uint32_t mask, uint32_t k) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(r) : "r"(x), "r"(mask), "r"(k));
+  return r;
+}
+
+// The four scale multipliers s * 2^-p (p = 0, 4, 8, 12) of one 128-group row.
+struct NibbleScales {
+  float s0, s4, s8, s12;
+};
+
+__device__ __forceinline__ NibbleScales nibble_scales(float s) {
+  return NibbleScales{s, s * 0.0625f, s * 0.00390625f, s * 0.000244140625f};
+}
+
+// 16 packed bytes = 32 int4 values -> 16 bf16x2 words, natural K order.
+// Each value is made a float by one LOP3 where it lies: nibble p of a word
+// (p = 0, 4, 8, 12; the upper four nibbles after one shift by 16) becomes
+// 2^23 + (q + 8) * 2^p, the bias 2^23 + 8 * 2^p is subtracted exactly and the
+// product with s * 2^-p -- exactly q * s before its one fp32 rounding -- is
+// rounded to bf16, as dequantize_tensor does.  Scales below 2^-100 (where
+// s * 2^-12 would lose bits) take the byte-permute form, which only divides by 16.
+__device__ __forceinline__ void dequant_int4_exact(uint4 v, float s, const NibbleScales& S, uint32_t (&out)[16]) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  if (s >= 0x1p-100f) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t y = w[i] >> 16;
+      out[i * 4 + 0] = scale_pair_to_bf16x2(and_xor(w[i], 0x0000000Fu, 0x4B000008u), and_xor(w[i], 0x000000F0u, 0x4B000080u),
+                                            -8388616.f, -8388736.f, S.s0, S.s4);
+      out[i * 4 + 1] = scale_pair_to_bf16x2(and_xor(w[i], 0x00000F00u, 0x4B000800u), and_xor(w[i], 0x0000F000u, 0x4B008000u),
+                                            -8390656.f, -8421376.f, S.s8, S.s12);
+      out[i * 4 + 2] = scale_pair_to_bf16x2(and_xor(y, 0x0000000Fu, 0x4B000008u), and_xor(y, 0x000000F0u, 0x4B000080u),
+                                            -8388616.f, -8388736.f, S.s0, S.s4);
+      out[i * 4 + 3] = scale_pair_to_bf16x2(and_xor(y, 0x00000F00u, 0x4B000800u), and_xor(y, 0x0000F000u, 0x4B008000u),
+                                            -8390656.f, -8421376.f, S.s8, S.s12);
+    }
+    return;
+  }
+  const float s16 = s * 0.0625f;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const uint32_t x = w[i] ^ 0x88888888u;
@@ -388,23 +451,26 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
                        const __grid_constant__ CUtensorMap tm_b12, const __grid_constant__ CUtensorMap tm_b13,
                        const TcArgs args) {
   using C = Cfg<GEMM1, BITS, FAST, NTM>;
-  constexpr int S = C::STAGES;
+  constexpr int WS = C::W_STAGES;
+  constexpr int BS = C::B_STAGES;
   constexpr int AS = C::A_STAGES;
   constexpr int SPLIT = C::SPLIT;
   constexpr int MMA_WARPS = C::MMA_WARPS;
   constexpr int DQ_WARPS = C::DQ_WARPS;
+  constexpr int FIRST_MMA = C::FIRST_MMA;
   constexpr int FIRST_DQ = C::FIRST_DQ;
   constexpr int FIRST_EPI = C::FIRST_EPI;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sw = smem;
-  uint8_t* sb = sw + S * C::W_STAGE_BYTES;
-  float* ssc = reinterpret_cast<float*>(sb + S * C::B_STAGE_BYTES);  // [2 bufs][2 tiles][128 * G]
+  uint8_t* sb = sw + WS * C::W_STAGE_BYTES;
+  float* ssc = reinterpret_cast<float*>(sb + BS * C::B_STAGE_BYTES);  // [2 bufs][2 tiles][128 * G]
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(ssc) + 2 * C::SCALE_BUF_BYTES);
-  uint64_t* full = bars;                // TMA data landed
-  uint64_t* wfree = full + S;           // dequant warps have read the weight tiles
-  uint64_t* mdone = wfree + S;          // the step's MMAs completed (one commit per step)
-  uint64_t* a_full = mdone + S;         // [2 tiles][AS]: TMEM A stage written
+  uint64_t* wfull = bars;               // [WS] weight tiles landed
+  uint64_t* wfree = wfull + WS;         // [WS] dequant warps have read the weight tiles
+  uint64_t* bfull = wfree + WS;         // [BS] token tile landed
+  uint64_t* mdone = bfull + BS;         // [BS] the step's MMAs completed (one commit per step)
+  uint64_t* a_full = mdone + BS;        // [2 tiles][AS]: TMEM A stage written
   uint64_t* sc_full = a_full + 2 * AS;  // [2]
   uint64_t* sc_empty = sc_full + 2;     // [2]
   uint64_t* acc_full = sc_empty + 2;    // [2] (per item in exact mode, per step in fast mode)
@@ -450,9 +516,12 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     if (lane == 31) tile_prefix[E] = incl;
   }
   if (threadIdx.x == 32) {
-    for (int i = 0; i < S; ++i) {
-      mbar_init(&full[i], 1);
+    for (int i = 0; i < WS; ++i) {
+      mbar_init(&wfull[i], 1);
       mbar_init(&wfree[i], DQ_WARPS);
+    }
+    for (int i = 0; i < BS; ++i) {
+      mbar_init(&bfull[i], 1);
       mbar_init(&mdone[i], MMA_WARPS);
     }
     for (int i = 0; i < 2 * AS; ++i) mbar_init(&a_full[i], DQ_WARPS / 2);  // per tile
@@ -466,7 +535,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
-  if (warp == 1) {
+  if (warp == FIRST_MMA) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(TMEM_COLS)
                  : "memory");
@@ -518,17 +587,56 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
   };
 
   if (warp == 0) {
-    // ------------------------------------------------------------- producer
+    // ------------------------------------------------------- weight producer
+    // per item the fp32 scales of both tiles, per K step both packed weight tiles
     if (lane == 0) {
-      int it = 0, issued = 0, rs = 0;
-      uint32_t rph = 0;  // ring slot and phase of step it
+      int issued = 0, rs = 0;
+      uint32_t rph = 0;  // weight ring slot and phase
       bool ok = true;
       for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
         const Item item = item_at(u);
         const TcPhase& P = args.ph[item.ph];
         const int G = P.groups;
         const int sbuf = ii & 1;
-        if (!mbar_wait_sleep(&sc_empty[sbuf], ((ii >> 1) & 1) ^ 1, abort_flag, 0x100)) break;
+        if (!mbar_wait(&sc_empty[sbuf], ((ii >> 1) & 1) ^ 1, abort_flag, 0x100)) break;
+        const uint32_t sbytes = static_cast<uint32_t>(ROWS * G * 4);
+        mbar_expect_tx(&sc_full[sbuf], 2 * sbytes);
+        float* sdst = ssc + sbuf * (2 * ROWS * MAX_G);
+        bulk_load(sdst, P.scale + wrow_of(item, 0) * G, sbytes, &sc_full[sbuf]);
+        bulk_load(sdst + ROWS * MAX_G, P.scale + wrow_of(item, 1) * G, sbytes, &sc_full[sbuf]);
+        const CUtensorMap* tw = item.ph == 0 ? &tm_w0 : &tm_w1;
+        const int w0 = static_cast<int>(wrow_of(item, 0)), w1 = static_cast<int>(wrow_of(item, 1));
+        int kbeg, kper;
+        k_range(item, kbeg, kper);
+        for (int kc = kbeg; kc < kbeg + kper; ++kc) {
+          if (!mbar_wait(&wfree[rs], rph ^ 1, abort_flag, 0x110 + rs)) { ok = false; break; }
+          mbar_expect_tx(&wfull[rs], C::W_STAGE_BYTES);
+          uint8_t* wdst = sw + rs * C::W_STAGE_BYTES;
+          tma_load_2d(wdst, tw, kc * C::W_ROW_BYTES, w0, &wfull[rs]);
+          tma_load_2d(wdst + C::W_TILE_BYTES, tw, kc * C::W_ROW_BYTES, w1, &wfull[rs]);
+          ++issued;
+          if (++rs == WS) {
+            rs = 0;
+            rph ^= 1;
+          }
+        }
+      }
+      // never leave copies in flight into this CTA's shared memory
+      for (int i = (issued > WS ? issued - WS : 0); i < issued; ++i) {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(&wfull[i % WS], (i / WS) & 1) && clock64() - t0 < kTimeoutCycles) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // -------------------------------------------------------- token producer
+    // per K step the token tile [rows x 128] bf16, into a slot the step's MMAs released
+    if (lane == 0) {
+      int issued = 0, rs = 0;
+      uint32_t rph = 0;  // token ring slot and phase
+      bool ok = true;
+      for (int u = blockIdx.x; u < total_items && ok; u += gridDim.x) {
+        const Item item = item_at(u);
         if (item.ph == 1) {
           // the GEMM1 items of this token tile (every epilogue warp of each) must have stored h
           const int need = args.ph[0].rblocks * C::EPI_WARPS;
@@ -546,56 +654,43 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           if (!ready) break;
           asm volatile("fence.proxy.async.global;" ::: "memory");  // generic stores of h -> TMA reads
         }
-        const uint32_t sbytes = static_cast<uint32_t>(ROWS * G * 4);
-        mbar_expect_tx(&sc_full[sbuf], 2 * sbytes);
-        float* sdst = ssc + sbuf * (2 * ROWS * MAX_G);
-        bulk_load(sdst, P.scale + wrow_of(item, 0) * G, sbytes, &sc_full[sbuf]);
-        bulk_load(sdst + ROWS * MAX_G, P.scale + wrow_of(item, 1) * G, sbytes, &sc_full[sbuf]);
         const int bi = box_index(item.rows_t);
         const int box = 16 << bi;
         const CUtensorMap* tb =
             item.ph == 0 ? (bi == 0 ? &tm_b00 : bi == 1 ? &tm_b01 : bi == 2 ? &tm_b02 : &tm_b03)
                          : (bi == 0 ? &tm_b10 : bi == 1 ? &tm_b11 : bi == 2 ? &tm_b12 : &tm_b13);
-        const CUtensorMap* tw = item.ph == 0 ? &tm_w0 : &tm_w1;
-        const int w0 = static_cast<int>(wrow_of(item, 0)), w1 = static_cast<int>(wrow_of(item, 1));
         int kbeg, kper;
         k_range(item, kbeg, kper);
-        for (int kc = kbeg; kc < kbeg + kper; ++kc, ++it) {
-          const int s = rs;
-          if (!mbar_wait_sleep(&wfree[s], rph ^ 1, abort_flag, 0x110 + s)) { ok = false; break; }
-          if (!mbar_wait_sleep(&mdone[s], rph ^ 1, abort_flag, 0x118 + s)) { ok = false; break; }
-          mbar_expect_tx(&full[s], C::W_STAGE_BYTES + 2 * box * 128);
-          uint8_t* wdst = sw + s * C::W_STAGE_BYTES;
-          tma_load_2d(wdst, tw, kc * C::W_ROW_BYTES, w0, &full[s]);
-          tma_load_2d(wdst + C::W_TILE_BYTES, tw, kc * C::W_ROW_BYTES, w1, &full[s]);
-          uint8_t* bdst = sb + s * C::B_STAGE_BYTES;
-          tma_load_2d(bdst, tb, kc * KC, item.row0, &full[s]);
-          tma_load_2d(bdst + box * 128, tb, kc * KC + 64, item.row0, &full[s]);
+        for (int kc = kbeg; kc < kbeg + kper; ++kc) {
+          if (!mbar_wait(&mdone[rs], rph ^ 1, abort_flag, 0x118 + rs)) { ok = false; break; }
+          mbar_expect_tx(&bfull[rs], 2 * box * 128);
+          uint8_t* bdst = sb + rs * C::B_STAGE_BYTES;
+          tma_load_2d(bdst, tb, kc * KC, item.row0, &bfull[rs]);
+          tma_load_2d(bdst + box * 128, tb, kc * KC + 64, item.row0, &bfull[rs]);
           ++issued;
-          if (++rs == S) {
+          if (++rs == BS) {
             rs = 0;
             rph ^= 1;
           }
         }
       }
-      // never leave copies in flight into this CTA's shared memory
-      for (int i = (issued > S ? issued - S : 0); i < issued; ++i) {
+      for (int i = (issued > BS ? issued - BS : 0); i < issued; ++i) {
         const long long t0 = clock64();
-        while (!mbar_try_wait(&full[i % S], (i / S) & 1) && clock64() - t0 < kTimeoutCycles) {
+        while (!mbar_try_wait(&bfull[i % BS], (i / BS) & 1) && clock64() - t0 < kTimeoutCycles) {
         }
       }
     }
   } else if (warp < FIRST_DQ) {
     // ------------------------------------------------------------- MMA issuers
-    const int tile = (warp - 1) & 1;      // weight tile
-    const int par = (warp - 1) >> 1;      // K-slice parity (SPLIT == 2)
+    const int tile = (warp - FIRST_MMA) & 1;   // weight tile
+    const int par = (warp - FIRST_MMA) >> 1;   // K-slice parity (SPLIT == 2)
     // the whole warp runs the loop (its descriptor arithmetic stays warp-uniform);
     // one elected lane issues the MMAs and the commits that track them
     const uint32_t leader = elect_one();
     {
       const uint32_t a_base = tmem + C::ACC_COLS;
       int it = 0, rs = 0, ra = 0;
-      uint32_t rph = 0, raph = 0;  // ring slot / phase and TMEM A stage / phase of step it
+      uint32_t rph = 0, raph = 0;  // token ring slot / phase and TMEM A stage / phase of step it
       bool ok = true;
       for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
         const Item item = item_at(u);
@@ -621,7 +716,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
             d0 = tmem + pb * 2 * NTM;
             d1 = d0 + NTM;
           }
-          if (!mbar_wait(&full[s], rph, abort_flag, 0x220 + s)) { ok = false; break; }
+          if (!mbar_wait(&bfull[s], rph, abort_flag, 0x220 + s)) { ok = false; break; }
           if (!mbar_wait(&a_full[tile * AS + sa], raph, abort_flag, 0x230 + sa)) { ok = false; break; }
           tc_fence_after();
           // descriptors advance by plain adds on the 16-byte-unit start address
@@ -635,11 +730,11 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
             const int j = jj * SPLIT + par;
             const uint64_t bdesc = bdesc0 + (j >> 2) * half_step + (j & 3) * 2;
             const uint32_t acc = jj > 0 ? 1u : first;
-            tc_mma(d, a_stage + j * 8, bdesc, idesc, acc, leader);
+            if (!LLQ_X_NOMMA) tc_mma(d, a_stage + j * 8, bdesc, idesc, acc, leader);
           }
           tc_commit(&mdone[s], leader);
           if (!FAST && kc == kend - 1) tc_commit(&acc_full[C::ACC_BUFS == 2 ? (ii & 1) : 0], leader);
-          if (++rs == S) {
+          if (++rs == BS) {
             rs = 0;
             rph ^= 1;
           }
@@ -659,8 +754,10 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     const int q = warp & 3;                 // TMEM lane quarter
     const int r = q * 32 + lane;            // row within the tile
     const uint32_t a_row = tmem + C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16) + wg * (KC / 2);
-    int it = 0, rs = 0, ps = S - AS, ra = 0;  // ring slots of steps it and it - AS, TMEM A stage of it
-    uint32_t rph = 0, pph = 1;                // their phases
+    // weight ring slot of step it, token ring slot of step it - AS (whose MMAs
+    // release TMEM A stage it % AS), TMEM A stage of step it, and their phases
+    int it = 0, rs = 0, ps = BS - AS, ra = 0;
+    uint32_t rph = 0, pph = 1;
     bool ok = true;
     for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
       const Item item = item_at(u);
@@ -674,7 +771,8 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
       for (int kc = kbeg; kc < kbeg + kper; ++kc, ++it) {
         const int s = rs, sa = ra;
         const float sc = FAST ? 0.f : srow[spg == 1 ? kc : spg == 0 ? 0 : kc / spg];
-        if (!mbar_wait(&full[s], rph, abort_flag, 0x310 + s)) { ok = false; break; }
+        const NibbleScales nsc = nibble_scales(sc);
+        if (!mbar_wait(&wfull[s], rph, abort_flag, 0x310 + s)) { ok = false; break; }
         const uint8_t* wt = sw + s * C::W_STAGE_BYTES + wg * C::W_TILE_BYTES + r * C::W_ROW_BYTES;
         const uint32_t a_stage = a_row + sa * C::A_STAGE_COLS;
         // this row's packed bytes into registers, then hand the weight slot back
@@ -696,8 +794,9 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
 #pragma unroll
           for (int ci = 0; ci < MYC; ++ci) {
             uint32_t o[16];
+            if (LLQ_X_NODQ) continue;
             if (FAST) codes_int4(v[ci], o);
-            else dequant_int4_exact(v[ci], sc, o);
+            else dequant_int4_exact(v[ci], sc, nsc, o);
             tc_st16(a_stage + (c_lo + ci) * 16, o);
           }
         } else {
@@ -713,11 +812,11 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[wg * AS + sa]);
-        if (++rs == S) {
+        if (++rs == WS) {
           rs = 0;
           rph ^= 1;
         }
-        if (++ps == S) {
+        if (++ps == BS) {
           ps = 0;
           pph ^= 1;
         }
@@ -742,8 +841,29 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
       const bool g1 = is_g1(item.ph);
       const int nt = (item.rows_t + 15) & ~15;
       const int t_begin = eg * (nt / EG), t_end = (eg + 1) * (nt / EG);
-      // one token's outputs from the two fp32 accumulators of row r
-      auto emit = [&](int t, float a0, float a1) {
+      // GEMM2: the (token, slot) destination and routed weight of this warp's tokens,
+      // one token per lane, loaded before the accumulators are ready and broadcast
+      // by shuffles below (a dependent pair of global loads per token otherwise)
+      constexpr int PER = (HALF + 31) / 32;
+      int32_t my_slot[PER];
+      float my_w[PER];
+      if (!g1 && args.ksplit <= 1) {
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+          const int t = t_begin + j * 32 + lane;
+          my_slot[j] = 0;
+          my_w[j] = 0.f;
+          if (t < t_end && t < item.rows_t) {
+            const int64_t p = static_cast<int64_t>(item.row0) + t;
+            my_slot[j] = args.sorted_slots != nullptr ? args.sorted_slots[p] : static_cast<int32_t>(p);
+            my_w[j] = args.topk_w != nullptr ? args.topk_w[my_slot[j]] : 1.f;
+          }
+        }
+      }
+      // one token's outputs from the two fp32 accumulators of row r (tl: token within
+      // this warp's share; warp-uniform, so the early return keeps the warp converged)
+      auto emit = [&](int tl, float a0, float a1) {
+        const int t = t_begin + tl;
         if (t >= t_end || t >= item.rows_t) return;
         const int64_t p = static_cast<int64_t>(item.row0) + t;
         if (g1) {
@@ -761,8 +881,8 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
             prow[ROWS] = a1;
             return;
           }
-          const int32_t slot = args.sorted_slots != nullptr ? args.sorted_slots[p] : static_cast<int32_t>(p);
-          const float w = args.topk_w != nullptr ? args.topk_w[slot] : 1.f;
+          const int32_t slot = __shfl_sync(0xffffffffu, my_slot[tl >> 5], tl & 31);
+          const float w = __shfl_sync(0xffffffffu, my_w[tl >> 5], tl & 31);
           __nv_bfloat16* orow;
           if (args.ep_on) {
             const int src = slot / args.ep.L.cap;
@@ -786,7 +906,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         const float* s1row = s0row + ROWS * MAX_G;
         for (int kc = 0; kc < P.K / KC; ++kc, ++it) {
           const int pb = it & 1;
-          if (!mbar_wait(&mdone[it % S], (it / S) & 1, abort_flag, 0x410 + pb)) { ok = false; break; }
+          if (!mbar_wait(&mdone[it % BS], (it / BS) & 1, abort_flag, 0x410 + pb)) { ok = false; break; }
           tc_fence_after();
           const int gi = P.group > 0 ? (kc * KC) / P.group : 0;
           const float s0 = s0row[gi], s1 = s1row[gi];
@@ -813,7 +933,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&sc_empty[sbuf]);
 #pragma unroll
-        for (int i = 0; i < (FAST ? HALF : 1); ++i) emit(t_begin + i, acc0[i], acc1[i]);
+        for (int i = 0; i < (FAST ? HALF : 1); ++i) emit(i, acc0[i], acc1[i]);
       } else {
         const int ab = C::ACC_BUFS == 2 ? (ii & 1) : 0;
         const uint32_t ph = C::ACC_BUFS == 2 ? ((ii >> 1) & 1) : (ii & 1);
@@ -838,7 +958,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
               }
             }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) emit(t0 + i, v0[i], v1[i]);
+            for (int i = 0; i < 8; ++i) emit(c * 8 + i, v0[i], v1[i]);
           }
         }
         tc_fence_before();
@@ -868,7 +988,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
       atomicExch(cta_done, 0);
     }
   }
-  if (warp == 1) {
+  if (warp == FIRST_MMA) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }
