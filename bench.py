@@ -5,7 +5,7 @@
 One step = one MoE layer forward (router + align + permute + W4A16 GEMM1 with
 SiLU + GEMM2 with routed weight + combine) over T=256 tokens (32 masked
 positions x batch 8, ~32 tokens/expert), E=64, H=2048, I=1024, top-8,
-INT4 group 128.  Synthetic seeded data: weights N(0,0.02)
+INT4 group 128 (the C3 layer).  Synthetic seeded data: weights N(0,0.02)
 bf16 quantized by this package's pack kernel, x ~ N(0,1) bf16, router N(0,0.02).
 Steps rotate over 4 distinct layer weight sets (855 MB > the 126 MB L2), so no
 step reads weights left in L2 by the previous one.
@@ -15,9 +15,19 @@ tokens per rank (weak scaling); rows travel by peer-memory stores through each
 rank's exchange window (``--ep-transport window``, the default) or by NCCL
 all-to-alls (``--ep-transport nccl``).
 
+Timing: the K-step region (barrier + synchronize on both sides, CUDA events,
+max over ranks) is repeated until at least one second of steps has been timed;
+``ms_per_step`` is the total over all repeats divided by their steps.  After
+every timed region the device error word (bounded waits that gave up) is read,
+and a non-zero word fails the run.
+
 At N = 1 the line also carries ``gpu_reference``: the reference's own PACKED
 algorithm on the same B200 -- dequantize every expert to BF16 (the property's
-fresh tensor per access) and a routed BF16 grouped matmul -- in torch ops.
+fresh tensor per access) and a routed BF16 grouped matmul -- in torch ops; and
+``c4``: the 16-layer stack over batch 32 x seq 1024 tokens (tensor-bound).
+At N > 1 it carries ``c5`` (the Zipf-skewed token sweep), ``phases`` (per-rank
+CUDA-event time of each exchange step, min and max over ranks) and
+``nccl_transport`` (the same layer over NCCL all-to-alls).
 
 ``--impl reference`` times the reference's CPU path (the numpy port of
 dequantize_tensor + the routed dequant-then-matmul, oracle/moe.py) on the host
@@ -64,6 +74,60 @@ def fused_bytes(n_rows: int, experts_hit: int) -> int:
     inside the launch's L2 working set and is not counted)."""
     per_expert = (2 * I * H // 2) + (2 * I * H // GROUP) * 4 + (H * I // 2) + (H * I // GROUP) * 4
     return experts_hit * per_expert + n_rows * H * 2 + n_rows * H * 2
+
+
+def bench_config(world: int, gemm: str, ep_transport: str, router_bias: str) -> dict:
+    """The workload description both arms print (identical dicts for the same command)."""
+    return {"workload": "C3 LLaDA-MoE-7B-A1B layer: E=64 H=2048 I=1024 top-8 W4A16 g128",
+            "tokens_per_rank": T_PER_RANK, "gemm": gemm,
+            "parallelism": "ep%d" % world if world > 1 else "single",
+            "ep_transport": (ep_transport if world > 1 else None),
+            "router_bias": router_bias,
+            "l2": "inputs larger than L2: 4 rotated layer weight sets (4 x 214 MB)"}
+
+
+MIN_TIMED_S = 1.0
+
+
+def timed_steps(step, steps: int, world: int, device, barrier, min_seconds: float = MIN_TIMED_S):
+    """Repeat the K-step region (barrier + synchronize on both sides, CUDA events) until at
+    least ``min_seconds`` of steps are timed.  Returns (ms per step, max over ranks; repeats;
+    seconds timed)."""
+    import torch
+    import torch.distributed as dist
+    total_ms, repeats = 0.0, 0
+    while True:
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(steps):
+            step(i)
+        b.record()
+        torch.cuda.synchronize()
+        barrier()
+        ms = a.elapsed_time(b)
+        if world > 1:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        total_ms += ms
+        repeats += 1
+        # ms is the max over ranks, so every rank takes the same decision
+        if total_ms >= min_seconds * 1e3 or repeats >= 100000:
+            break
+    return total_ms / (repeats * steps), repeats, total_ms / 1e3
+
+
+def check_device_error(where: str) -> int:
+    """Read the library's device error word after a timed region; a non-zero word (a bounded
+    wait that gave up) fails the run."""
+    from llada_quant_b200 import ops
+    code = ops.device_error()
+    if code != 0:
+        raise SystemExit(f"bench: device error word 0x{code:x} after {where}")
+    return code
 
 
 def read_peaks():
@@ -214,8 +278,7 @@ def run_reference(args, rank: int):
         "warmup": args.warmup, "ms_per_step": T_PER_RANK / value * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, bf16 activations, fp32 accumulate",
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) tokens)", "impl": "reference",
-        "config": {"workload": "C3 LLaDA-MoE-7B-A1B layer: E=64 H=2048 I=1024 top-8 W4A16 g128",
-                   "tokens_per_step": T_PER_RANK},
+        "config": bench_config(args.gpus, args.gemm, args.ep_transport, args.router_bias),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
                          "sample": "one C3 layer call (256 tokens) per step: "
                                    + ("the reference's own dequantize_tensor (baseline/_ref) in torch on the host"
@@ -347,12 +410,12 @@ def time_gpu_reference(xs, gate_w, layers, args, device):
     else:
         eager = lambda q, sc: _ref_dequantize(q, sc, BITS)
         source = "restatement of dequantize_tensor in torch ops (baseline/_ref not installed)"
-    grouped = True
+    grouped, grouped_error = True, None
     try:
         _ref_layer(xs[0], gate_w, layers[0], True, eager)
         torch.cuda.synchronize()
-    except Exception:
-        grouped = False
+    except Exception as exc:  # recorded in the line, never hidden
+        grouped, grouped_error = False, f"{type(exc).__name__}: {exc}"[:300]
     steps = max(3, min(args.steps, 10))
     out = {}
     variants = [("eager", eager)]
@@ -377,7 +440,8 @@ def time_gpu_reference(xs, gate_w, layers, args, device):
     line = {"source": source,
             "method": "PACKED dequantize of w1/w2 to bf16 per call + "
                       + ("torch._grouped_mm" if grouped else "per-expert torch matmul") + " (bf16)",
-            "rel_l2_vs_ours": float((ours - ref).norm() / ref.norm()), "variants": out}
+            "rel_l2_vs_ours": float((ours - ref).norm() / ref.norm()), "variants": out,
+            "grouped_mm_error": grouped_error}
     if best is not None:
         line.update(value=best["value"], unit=UNIT, ms_per_step=best["ms_per_step"])
     return line
@@ -412,6 +476,85 @@ def time_w8a16_comparator(device):
                      "rel_l2": float((y_ours - y_ref).norm() / y_ref.norm())})
     return {"shape": {"K": K, "N": N, "bits": 8, "group": 128}, "rows": rows,
             "note": "per call, host-launched (both sides pay their launch overhead)"}
+
+
+def phase_breakdown(call, n: int, world: int, device) -> dict:
+    """Per-phase CUDA-event time of ``n`` layer calls (``call(i, marks)`` appends (name, event)
+    pairs), averaged per call on each rank, then the min and max over ranks of each phase."""
+    import torch
+    import torch.distributed as dist
+    runs = []
+    for i in range(n):
+        marks = []
+        call(i, marks)
+        runs.append(marks)
+    torch.cuda.synchronize()
+    names = [m[0] for m in runs[0][1:]]
+    per = torch.zeros(len(names), dtype=torch.float64)
+    for marks in runs:
+        for j in range(1, len(marks)):
+            per[j - 1] += marks[j - 1][1].elapsed_time(marks[j][1])
+    per /= n
+    per = per.to(device)
+    if world > 1:
+        lo, hi = per.clone(), per.clone()
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+    else:
+        lo = hi = per
+    lo, hi = lo.tolist(), hi.tolist()
+    return {name: {"ms_min": round(lo[j], 4), "ms_max": round(hi[j], 4)} for j, name in enumerate(names)}
+
+
+def c5_sweep(args, world: int, rank: int, device, layers, gate_w, barrier) -> list:
+    """The C5 workload at this world size: the C3 layer expert-parallel with the Zipf(1.1)
+    router bias b_e = -1.1 ln(rank_e), T tokens per rank for T in 256..65536 (a point is
+    skipped, with its reason, when its exchange window would not fit in free memory).
+    Tokens/s of the whole job, ms per layer (max over ranks), the HBM fraction of the layer
+    bytes each rank reads (its expert shard) and the tensor fraction of the layer FLOPs."""
+    import torch
+    import torch.distributed as dist
+    from llada_quant_b200 import ep, ops
+    from llada_quant_b200.fused_moe import IMPL
+    impl = IMPL[args.gemm]
+    rank_e = torch.randperm(E, generator=torch.Generator().manual_seed(3)).to(torch.float32) + 1.0
+    bias = (-1.1 * torch.log(rank_e)).to(device)
+    hbm, _ = read_peaks()
+    tflops_peak, _ = read_tensor_peak()
+    E_local = E // world
+    shard_bytes = E_local * ((2 * I * H // 2) + (2 * I * H // GROUP) * 4 + (H * I // 2) + (H * I // GROUP) * 4)
+    out = []
+    for T in (256, 1024, 4096, 16384, 65536):
+        need = 2 * world * T * TOPK * H * 2 + 6 * T * TOPK * max(H, I) * 2
+        free = torch.tensor([float(torch.cuda.mem_get_info(device)[0])], device=device)
+        if world > 1:
+            dist.all_reduce(free, op=dist.ReduceOp.MIN)
+        if need > 0.8 * float(free.item()):
+            out.append({"T_per_rank": T, "skipped": f"needs ~{need / 2**30:.1f} GiB of exchange buffers"})
+            continue
+        g = torch.Generator(device=device).manual_seed(50 + rank)
+        xs = [torch.randn(T, H, generator=g, device=device).to(torch.bfloat16) for _ in range(2)]
+        window = ep.EPWindow(T, TOPK, H, rank, world, device) if args.ep_transport == "window" else None
+
+        def step(i):
+            return ep.ep_moe_layer(xs[i & 1], gate_w, layers[i % N_LAYERS], TOPK, rank, world, bias=bias,
+                                   impl=impl, window=window)
+        ops.clear_device_error()
+        for i in range(2):
+            step(i)
+        steps = 10 if T <= 4096 else 4
+        ms, repeats, timed_s = timed_steps(step, steps, world, device, barrier, min_seconds=0.3)
+        dev_err = check_device_error(f"the C5 region at T={T}")
+        flops = 2.0 * T * world * TOPK * (2 * I * H + H * I) / world  # per rank, balanced share
+        out.append({"T_per_rank": T, "tokens_per_s": T * world / (ms / 1e3), "ms_per_step": round(ms, 4),
+                    "hbm_frac": round(shard_bytes / (ms / 1e3) / 1e9 / hbm, 4),
+                    "tensor_frac": round(flops / (ms / 1e3) / 1e12 / tflops_peak, 4),
+                    "timed_region_s": round(timed_s, 3), "device_error": dev_err})
+        if window is not None:
+            window.close()
+        del xs
+        torch.cuda.empty_cache()
+    return out
 
 
 def run_ours(args, rank: int, world: int, local_rank: int):
@@ -455,25 +598,12 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             dist.barrier()
 
     # ---- warm-up + timed device region -------------------------------------------
+    ops.clear_device_error()
     for i in range(args.warmup):
         step(i)
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
-        start.record()
-        for i in range(args.steps):
-            step(i)
-        end.record()
-        torch.cuda.synchronize()
-    barrier()
-    ms = start.elapsed_time(end)
-    if world > 1:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    ms_per_step = ms / args.steps
+        ms_per_step, repeats, timed_s = timed_steps(step, args.steps, world, device, barrier)
+    dev_err = check_device_error("the timed device region")
     tokens_per_step = T_PER_RANK * world
     value = tokens_per_step / (ms_per_step / 1e3)
 
@@ -535,19 +665,26 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
     e2e_run(args.warmup)
     torch.cuda.synchronize()
-    barrier()
-    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record(comp)
-    e2e_run(args.steps, start=s2)
-    e2.record(comp)
-    torch.cuda.synchronize()
-    barrier()
-    ms_e2e = s2.elapsed_time(e2)
-    if world > 1:
-        t = torch.tensor([ms_e2e], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_e2e = float(t.item())
-    e2e_value = tokens_per_step / (ms_e2e / args.steps / 1e3)
+    ms_e2e_total, e2e_repeats = 0.0, 0
+    while ms_e2e_total < MIN_TIMED_S * 1e3:
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record(comp)
+        e2e_run(args.steps, start=s2)
+        e2.record(comp)
+        torch.cuda.synchronize()
+        barrier()
+        ms_e2e = s2.elapsed_time(e2)
+        if world > 1:
+            t = torch.tensor([ms_e2e], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_e2e = float(t.item())
+        ms_e2e_total += ms_e2e
+        e2e_repeats += 1
+    check_device_error("the end-to-end region")
+    e2e_value = tokens_per_step / (ms_e2e_total / (e2e_repeats * args.steps) / 1e3)
 
     # ---- dominant kernel (the fused expert GEMMs) timed alone with CUDA events ---------
     kernel = None
@@ -570,14 +707,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         for l in range(N_LAYERS):
             run(l)
         torch.cuda.synchronize()
-        reps = max(args.steps, 8)
-        ks, ke = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ks.record()
-        for i in range(reps):
-            run(i % N_LAYERS)
-        ke.record()
-        torch.cuda.synchronize()
-        k_ms = ks.elapsed_time(ke) / reps
+        k_ms, _, _ = timed_steps(lambda i: run(i % N_LAYERS), max(args.steps, 8), 1, device, barrier)
+        check_device_error("the dominant-kernel region")
         hit = int(round(statistics.mean(p[4] for p in preps)))
         algo = fused_bytes(n_rows, hit) if fused else gemm1_bytes(n_rows, hit)
         peak, peak_kind = read_peaks()
@@ -599,6 +730,35 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         gpu_ref = time_gpu_reference(xs, gate_w, layers, args, device)
         w8a16 = time_w8a16_comparator(device)
 
+    # ---- the other BASELINE workloads at this world size ------------------------------
+    extras = {}
+    if world == 1 and not args.no_c4:
+        extras["c4"] = measure_c4(args, steps=3, warmup=1)
+    if world > 1:
+        from llada_quant_b200 import ep as _ep
+        extras["phases"] = {
+            "transport": args.ep_transport,
+            "per_layer": phase_breakdown(
+                lambda i, m: _ep.ep_moe_layer(xs[i % N_LAYERS], gate_w, layers[i % N_LAYERS], TOPK, rank, world,
+                                              bias=bias, impl=impl, window=window, marks=m), 20, world, device)}
+        if args.ep_transport == "window":
+            # the same layer over NCCL all-to-alls, on the same box, for comparison
+            nccl_step = lambda i: _ep.ep_moe_layer(xs[i % N_LAYERS], gate_w, layers[i % N_LAYERS], TOPK, rank,
+                                                   world, bias=bias, impl=impl, window=None)
+            for i in range(3):
+                nccl_step(i)
+            ms_n, rep_n, ts_n = timed_steps(nccl_step, args.steps, world, device, barrier, min_seconds=0.5)
+            check_device_error("the NCCL-transport region")
+            extras["nccl_transport"] = {
+                "value": tokens_per_step / (ms_n / 1e3), "unit": UNIT, "ms_per_step": ms_n,
+                "timed_region_s": round(ts_n, 3),
+                "phases": phase_breakdown(
+                    lambda i, m: _ep.ep_moe_layer(xs[i % N_LAYERS], gate_w, layers[i % N_LAYERS], TOPK, rank,
+                                                  world, bias=bias, impl=impl, window=None, marks=m),
+                    10, world, device)}
+        if not args.no_c5:
+            extras["c5"] = c5_sweep(args, world, rank, device, layers, gate_w, barrier)
+
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu:
@@ -618,17 +778,13 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, bf16 activations, fp32 accumulate",
             "data": "synthetic (seeded N(0,0.02) weights quantized on device, N(0,1) tokens)",
-            "config": {"workload": "C3 LLaDA-MoE-7B-A1B layer: E=64 H=2048 I=1024 top-8 W4A16 g128",
-                       "tokens_per_rank": T_PER_RANK, "gemm": args.gemm,
-                       "parallelism": "ep%d" % world if world > 1 else "single",
-                       "ep_transport": (args.ep_transport if world > 1 else None),
-                       "router_bias": args.router_bias,
-                       "l2": "inputs larger than L2: 4 rotated layer weight sets (4 x 214 MB)"},
+            "config": bench_config(world, args.gemm, args.ep_transport, args.router_bias),
+            "timing": {"repeats": repeats, "timed_region_s": round(timed_s, 3), "device_error": dev_err},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T_PER_RANK * H * 2,
                     "d2h_bytes_per_step": T_PER_RANK * H * 2,
                     "copies": "pinned host <-> device every step, on their own streams, overlapped with the "
                               "neighbouring steps' layers"},
-            "gpu_launches": (launches_per_step * args.steps) if launches_per_step else None,
+            "gpu_launches": launches_per_step * args.steps * repeats,
             "roofline": kernel,
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
@@ -637,6 +793,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             line["gpu_reference"] = gpu_ref
         if w8a16 is not None:
             line["gpu_reference_w8a16_gemm"] = w8a16
+        line.update(extras)
         print(json.dumps(line), flush=True)
     if window is not None:
         window.close()
@@ -651,10 +808,18 @@ def c4_flops() -> float:
     return per_layer * C4_LAYERS
 
 
-def run_c4(args):
-    """16 chained C3-shaped layers (x <- x + moe_l(x)) over 32768 tokens on one
-    GPU; attention/norms are outside the hot path and not modelled.  Metric: tokens/s of the stack,
-    with TFLOP/s against the measured dense bf16 peak."""
+def read_tensor_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops_sustained"]), "measured (sustained)"
+    except Exception:
+        return 1400.0, "fallback (sustained)"
+
+
+def measure_c4(args, steps: int, warmup: int) -> dict:
+    """The C4 workload: 16 chained C3-shaped layers (x <- x + moe_l(x)) over 32768 tokens on one
+    GPU; attention/norms are outside the hot path and not modelled.  Tokens/s of the stack, with
+    TFLOP/s against the measured sustained dense bf16 peak (a seconds-long step)."""
     import torch
     from llada_quant_b200 import ops
     from llada_quant_b200.fused_moe import IMPL
@@ -665,7 +830,7 @@ def run_c4(args):
                      device=device).to(torch.bfloat16)
     impl = IMPL[args.gemm]
 
-    def step():
+    def step(_i=0):
         x = x0
         for lay in layers:
             tw, ids, _ = ops._route_impl(x, gate_w, TOPK, None, False)
@@ -673,38 +838,41 @@ def run_c4(args):
             x = x + y
         return x
 
-    for _ in range(args.warmup):
+    ops.clear_device_error()
+    for _ in range(warmup):
         step()
-    torch.cuda.synchronize()
-    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(0) as clocks:
-        s0.record()
-        for _ in range(args.steps):
-            step()
-        s1.record()
-        torch.cuda.synchronize()
-    ms = s0.elapsed_time(s1) / args.steps
+        ms, repeats, timed_s = timed_steps(step, steps, 1, device, lambda: None)
+    dev_err = check_device_error("the C4 region")
     tflops = c4_flops() / (ms / 1e3) / 1e12
-    peak = None
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            peak = float(json.load(f)["bf16_tflops_sustained"])
-        kind = "measured (sustained)"
-    except Exception:
-        peak, kind = 1400.0, "fallback (sustained)"
+    peak, kind = read_tensor_peak()
+    out = {"workload": "C4 16-layer MoE stack, T=32768 (batch 32 x seq 1024), E=64 H=2048 I=1024 top-8 W4A16 g128",
+           "value": C4_TOKENS / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+           "repeats": repeats, "timed_region_s": round(timed_s, 3), "device_error": dev_err,
+           "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                        "frac": round(tflops / peak, 4), "peak_source": kind, "algorithmic_flops": c4_flops()},
+           "clocks": clocks.summary()}
+    del layers
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_c4(args):
+    """--workload c4: the C4 stack as its own bench line."""
+    c4 = measure_c4(args, args.steps, args.warmup)
     line = {
         "metric": "W4A16 MoE stack tokens/s (LLaDA-MoE-7B-A1B, 16 layers, batch 32 x seq 1024)",
-        "value": C4_TOKENS / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "value": c4["value"], "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": c4["ms_per_step"], "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int4 weights, bf16 activations, fp32 accumulate",
         "data": "synthetic (seeded N(0,0.02) weights quantized on device, N(0,1) tokens)",
-        "config": {"workload": "C4 16-layer MoE stack, T=32768, E=64 H=2048 I=1024 top-8 W4A16 g128",
-                   "gemm": args.gemm, "l2": "inputs larger than L2 (16 layer weight sets, 3.4 GB)"},
-        "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
-                     "frac": round(tflops / peak, 4), "peak_source": kind, "traffic": None,
-                     "algorithmic_flops": c4_flops()},
-        "gpu_launches": 7 * C4_LAYERS * args.steps,
-        "clocks": clocks.summary(),
+        "config": {"workload": c4["workload"], "gemm": args.gemm,
+                   "l2": "inputs larger than L2 (16 layer weight sets, 3.4 GB)"},
+        "roofline": dict(c4["roofline"], traffic=None),
+        "gpu_launches": 7 * C4_LAYERS * args.steps * c4["repeats"],
+        "timing": {"repeats": c4["repeats"], "timed_region_s": c4["timed_region_s"],
+                   "device_error": c4["device_error"]},
+        "clocks": c4["clocks"],
     }
     print(json.dumps(line), flush=True)
 
@@ -744,6 +912,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--gemm", choices=["auto", "tcgen05", "tcgen05_fast", "simt"], default="auto")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-c4", action="store_true", help="N=1: skip the C4 stack measurement")
+    ap.add_argument("--no-c5", action="store_true", help="N>1: skip the C5 token sweep")
     ap.add_argument("--no-gpu-ref", action="store_true",
                     help="skip the reference-algorithm-on-B200 leg (dequantize + BF16 matmul)")
     ap.add_argument("--ep-transport", choices=["window", "nccl"], default="window",

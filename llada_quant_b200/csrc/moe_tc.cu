@@ -48,11 +48,24 @@
 #ifndef LLQ_X_NODQ
 #define LLQ_X_NODQ 0
 #endif
+#ifndef LLQ_X_PROF
+#define LLQ_X_PROF 0
+#endif
+#if LLQ_X_PROF
+__device__ long long g_xprof[256][48];
+#define XP_INIT long long xp_acc[8] = {0, 0, 0, 0, 0, 0, 0, 0}; long long xp_last = clock64();
+#define XP(i) do { const long long xp_n = clock64(); xp_acc[i] += xp_n - xp_last; xp_last = xp_n; } while (0)
+#define XP_SAVE(role) do { if (lane == 0) for (int xi = 0; xi < 8; ++xi) g_xprof[blockIdx.x][(role) * 8 + xi] = xp_acc[xi]; } while (0)
+#else
+#define XP_INIT
+#define XP(i) do {} while (0)
+#define XP_SAVE(role) do {} while (0)
+#endif
 #ifndef LLQ_X_SPLIT
 #define LLQ_X_SPLIT 1
 #endif
-#ifndef LLQ_X_DQW
-#define LLQ_X_DQW 8
+#ifndef LLQ_X_DQG
+#define LLQ_X_DQG 1
 #endif
 #ifndef LLQ_X_EPW
 #define LLQ_X_EPW 8
@@ -70,8 +83,12 @@ constexpr long long kTimeoutCycles = 4000000000LL;
 
 template <bool GEMM1, int BITS, bool FAST, int NTM>
 struct Cfg {
-  static constexpr int W_ROW_BYTES = KC * BITS / 8;
-  static constexpr int W_TILE_BYTES = ROWS * W_ROW_BYTES;
+  static constexpr int W_ROW_BYTES = KC * BITS / 8;  // packed bytes of one row per K step
+  // a weight load brings 128 bytes of each row (two K steps at INT4): twice the
+  // DRAM burst of one step, half the TMA row requests per weight byte
+  static constexpr int W_STEPS = 128 / W_ROW_BYTES;
+  static constexpr int W_LOAD_BYTES = W_ROW_BYTES * W_STEPS;
+  static constexpr int W_TILE_BYTES = ROWS * W_LOAD_BYTES;
   static constexpr int W_STAGE_BYTES = 2 * W_TILE_BYTES;
   static constexpr int B_STAGE_BYTES = NTM * KC * 2;
   static constexpr int SCALE_BUF_BYTES = 2 * ROWS * MAX_G * 4;
@@ -79,7 +96,7 @@ struct Cfg {
   // copied them to registers, and token tiles, released when the step's MMAs
   // complete.  Weight slots thus turn over at the speed of HBM, independently
   // of the MMA pipeline, and the weight ring takes what shared memory is left.
-  static constexpr int B_STAGES = B_STAGE_BYTES <= 16384 ? 4 : 3;
+  static constexpr int B_STAGES = 3;
   static constexpr int W_STAGES_FIT =
       (220 * 1024 - 2 * SCALE_BUF_BYTES - B_STAGES * B_STAGE_BYTES) / W_STAGE_BYTES;
   static constexpr int W_STAGES = W_STAGES_FIT > 8 ? 8 : W_STAGES_FIT;
@@ -95,9 +112,11 @@ struct Cfg {
   static constexpr int MMA_WARPS = 2 * SPLIT;
   // (measured at C3: 16 dequantizing warps with one epilogue warpgroup made
   // the exact GEMM1 11% slower than 8 + 8; the code supports both)
-  static constexpr int DQ_WARPS = LLQ_X_DQW;
+  // dequantizing warps: DQ_GROUPS groups of 8 (one warpgroup per weight tile)
+  // that take alternate K steps, so that one group's waits overlap the other's math
+  static constexpr int DQ_GROUPS = FAST ? 1 : LLQ_X_DQG;
+  static constexpr int DQ_WARPS = 8 * DQ_GROUPS;
   static constexpr int EPI_WARPS = LLQ_X_EPW;  // token groups of one warpgroup each
-  static constexpr int DQ_PARTS = DQ_WARPS / 8;  // warpgroups per weight tile
   static constexpr int FIRST_MMA = 2;  // warp 0 loads weights and scales, warp 1 token tiles
   static constexpr int FIRST_DQ = FIRST_MMA + MMA_WARPS;
   static constexpr int FIRST_EPI = FIRST_DQ + DQ_WARPS;
@@ -114,7 +133,7 @@ struct Cfg {
   static constexpr int CHUNKS = W_ROW_BYTES / 16;
   static constexpr size_t SMEM_BYTES =
       1024 + static_cast<size_t>(W_STAGES) * W_STAGE_BYTES + static_cast<size_t>(B_STAGES) * B_STAGE_BYTES +
-      2 * SCALE_BUF_BYTES + 2048;
+      2 * SCALE_BUF_BYTES + 4096;
   static_assert(W_STAGES >= 2 && B_STAGES >= 2 && A_STAGES >= 2, "pipeline too shallow");
   static_assert(A_STAGES <= B_STAGES, "a TMEM A stage is released through the token ring");
   static_assert(!FAST || BITS == 4, "fast mode is INT4 only");
@@ -181,41 +200,37 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that suspends the thread in hardware until the phase completes or
+// `ns` nanoseconds pass, so that waiting warps take no issue slots from the
+// dequantizing warps that share their SM sub-partition
+__device__ __forceinline__ bool mbar_try_wait_for(uint64_t* b, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
+constexpr uint32_t kSuspendNs = 200000;  // one suspended try_wait, 0.2 ms at most
+
 // Bounded wait: false if the CTA is aborting or the wait timed out (then it
 // records `code` in the device error word and raises the CTA's abort flag).
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag,
                                           int code) {
-  if (mbar_try_wait(b, parity)) return true;
+  if (mbar_try_wait_for(b, parity, kSuspendNs)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try_wait(b, parity)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > kTimeoutCycles) {
       *abort_flag = 1;
       atomicExch(&g_device_error, code);
       return false;
     }
-  }
-}
-
-// Same, for waits off the critical path (producer slots, epilogue hand-offs):
-// backs off with nanosleep so that a waiting warp does not take issue slots
-// from the dequantizing warps on its SM sub-partition.
-__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* b, uint32_t parity, volatile int* abort_flag,
-                                                int code) {
-  if (mbar_try_wait(b, parity)) return true;
-  const long long t0 = clock64();
-  unsigned ns = 32;
-  while (true) {
-    __nanosleep(ns);
-    if (ns < 256) ns <<= 1;
-    if (mbar_try_wait(b, parity)) return true;
-    if (*abort_flag) return false;
-    if (clock64() - t0 > kTimeoutCycles) {
-      *abort_flag = 1;
-      atomicExch(&g_device_error, code);
-      return false;
-    }
+    if (mbar_try_wait_for(b, parity, kSuspendNs)) return true;
   }
 }
 
@@ -286,6 +301,7 @@ __device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&v)[16])
 
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// 8 consecutive fp32 columns of this thread's TMEM lane; complete after tc_wait_ld()
 __device__ __forceinline__ void tc_ld8(uint32_t taddr, float (&v)[8]) {
   uint32_t r[8];
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
@@ -293,10 +309,25 @@ __device__ __forceinline__ void tc_ld8(uint32_t taddr, float (&v)[8]) {
                  "=r"(r[7])
                : "r"(taddr)
                : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
+
+// 16 consecutive fp32 columns of this thread's TMEM lane; complete after tc_wait_ld()
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // instruction descriptor: D f32, A/B bf16, both K-major, M = 128, N = n
 __device__ __forceinline__ uint32_t make_idesc(int n) {
@@ -478,6 +509,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* tile_prefix = reinterpret_cast<int*>(tmem_slot + 2);  // [E + 1]
+  int* row_offsets = tile_prefix + MAX_E + 1;                // [E + 1]: the expert offsets, staged once
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = args.E;
@@ -494,7 +526,10 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
       const int e = lane * (MAX_E / 32) + j;
       int n = 0;
       if (e < E) {
-        const int m = args.offsets != nullptr ? args.offsets[e + 1] - args.offsets[e] : args.dense_rows;
+        const int o0 = args.offsets != nullptr ? args.offsets[e] : 0;
+        const int m = args.offsets != nullptr ? args.offsets[e + 1] - o0 : args.dense_rows;
+        row_offsets[e] = o0;
+        if (e == E - 1) row_offsets[E] = o0 + m;
         n = (m + NTM - 1) / NTM;
       }
       local[j] = n;
@@ -524,7 +559,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
       mbar_init(&bfull[i], 1);
       mbar_init(&mdone[i], MMA_WARPS);
     }
-    for (int i = 0; i < 2 * AS; ++i) mbar_init(&a_full[i], DQ_WARPS / 2);  // per tile
+    for (int i = 0; i < 2 * AS; ++i) mbar_init(&a_full[i], 4);  // the tile's warpgroup of the step's group
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sc_full[i], 1);
       mbar_init(&sc_empty[i], FAST ? DQ_WARPS + C::EPI_WARPS : DQ_WARPS);
@@ -567,8 +602,8 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     }
     it.e = lo;
     it.tt = tg - tile_prefix[lo];
-    const int base = args.offsets != nullptr ? args.offsets[lo] : 0;
-    const int m = args.offsets != nullptr ? args.offsets[lo + 1] - base : args.dense_rows;
+    const int base = row_offsets[lo];
+    const int m = row_offsets[lo + 1] - base;
     it.row0 = base + it.tt * NTM;
     it.rows_t = min(NTM, m - it.tt * NTM);
     return it;
@@ -590,6 +625,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     // ------------------------------------------------------- weight producer
     // per item the fp32 scales of both tiles, per K step both packed weight tiles
     if (lane == 0) {
+      XP_INIT
       int issued = 0, rs = 0;
       uint32_t rph = 0;  // weight ring slot and phase
       bool ok = true;
@@ -604,16 +640,20 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         float* sdst = ssc + sbuf * (2 * ROWS * MAX_G);
         bulk_load(sdst, P.scale + wrow_of(item, 0) * G, sbytes, &sc_full[sbuf]);
         bulk_load(sdst + ROWS * MAX_G, P.scale + wrow_of(item, 1) * G, sbytes, &sc_full[sbuf]);
+        XP(0);
         const CUtensorMap* tw = item.ph == 0 ? &tm_w0 : &tm_w1;
         const int w0 = static_cast<int>(wrow_of(item, 0)), w1 = static_cast<int>(wrow_of(item, 1));
         int kbeg, kper;
         k_range(item, kbeg, kper);
-        for (int kc = kbeg; kc < kbeg + kper; ++kc) {
+        for (int kc = kbeg; kc < kbeg + kper; kc += C::W_STEPS) {
+          XP(3);
           if (!mbar_wait(&wfree[rs], rph ^ 1, abort_flag, 0x110 + rs)) { ok = false; break; }
+          XP(1);
           mbar_expect_tx(&wfull[rs], C::W_STAGE_BYTES);
           uint8_t* wdst = sw + rs * C::W_STAGE_BYTES;
           tma_load_2d(wdst, tw, kc * C::W_ROW_BYTES, w0, &wfull[rs]);
           tma_load_2d(wdst + C::W_TILE_BYTES, tw, kc * C::W_ROW_BYTES, w1, &wfull[rs]);
+          XP(2);
           ++issued;
           if (++rs == WS) {
             rs = 0;
@@ -621,6 +661,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           }
         }
       }
+      XP_SAVE(0);
       // never leave copies in flight into this CTA's shared memory
       for (int i = (issued > WS ? issued - WS : 0); i < issued; ++i) {
         const long long t0 = clock64();
@@ -632,6 +673,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     // -------------------------------------------------------- token producer
     // per K step the token tile [rows x 128] bf16, into a slot the step's MMAs released
     if (lane == 0) {
+      XP_INIT
       int issued = 0, rs = 0;
       uint32_t rph = 0;  // token ring slot and phase
       bool ok = true;
@@ -654,6 +696,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           if (!ready) break;
           asm volatile("fence.proxy.async.global;" ::: "memory");  // generic stores of h -> TMA reads
         }
+        XP(0);
         const int bi = box_index(item.rows_t);
         const int box = 16 << bi;
         const CUtensorMap* tb =
@@ -662,11 +705,14 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         int kbeg, kper;
         k_range(item, kbeg, kper);
         for (int kc = kbeg; kc < kbeg + kper; ++kc) {
+          XP(3);
           if (!mbar_wait(&mdone[rs], rph ^ 1, abort_flag, 0x118 + rs)) { ok = false; break; }
+          XP(1);
           mbar_expect_tx(&bfull[rs], 2 * box * 128);
           uint8_t* bdst = sb + rs * C::B_STAGE_BYTES;
           tma_load_2d(bdst, tb, kc * KC, item.row0, &bfull[rs]);
           tma_load_2d(bdst + box * 128, tb, kc * KC + 64, item.row0, &bfull[rs]);
+          XP(2);
           ++issued;
           if (++rs == BS) {
             rs = 0;
@@ -674,6 +720,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           }
         }
       }
+      XP_SAVE(1);
       for (int i = (issued > BS ? issued - BS : 0); i < issued; ++i) {
         const long long t0 = clock64();
         while (!mbar_try_wait(&bfull[i % BS], (i / BS) & 1) && clock64() - t0 < kTimeoutCycles) {
@@ -687,6 +734,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     // the whole warp runs the loop (its descriptor arithmetic stays warp-uniform);
     // one elected lane issues the MMAs and the commits that track them
     const uint32_t leader = elect_one();
+    XP_INIT
     {
       const uint32_t a_base = tmem + C::ACC_COLS;
       int it = 0, rs = 0, ra = 0;
@@ -700,8 +748,10 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         if (!FAST) {
           const int ab = C::ACC_BUFS == 2 ? (ii & 1) : 0;
           const uint32_t ph = C::ACC_BUFS == 2 ? ((ii >> 1) & 1) : (ii & 1);
-          if (!mbar_wait_sleep(&acc_empty[ab], ph ^ 1, abort_flag, 0x200)) break;
+          XP(4);
+          if (!mbar_wait(&acc_empty[ab], ph ^ 1, abort_flag, 0x200)) break;
           tc_fence_after();
+          XP(0);
         }
         int kbeg, kper;
         k_range(item, kbeg, kper);
@@ -716,8 +766,11 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
             d0 = tmem + pb * 2 * NTM;
             d1 = d0 + NTM;
           }
+          XP(4);
           if (!mbar_wait(&bfull[s], rph, abort_flag, 0x220 + s)) { ok = false; break; }
+          XP(1);
           if (!mbar_wait(&a_full[tile * AS + sa], raph, abort_flag, 0x230 + sa)) { ok = false; break; }
+          XP(2);
           tc_fence_after();
           // descriptors advance by plain adds on the 16-byte-unit start address
           const uint64_t bdesc0 = make_sdesc(smem_u32(sb + s * C::B_STAGE_BYTES));
@@ -734,6 +787,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           }
           tc_commit(&mdone[s], leader);
           if (!FAST && kc == kend - 1) tc_commit(&acc_full[C::ACC_BUFS == 2 ? (ii & 1) : 0], leader);
+          XP(3);
           if (++rs == BS) {
             rs = 0;
             rph ^= 1;
@@ -745,12 +799,11 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         }
       }
     }
+    if (warp == FIRST_MMA) XP_SAVE(2);
   } else if (warp < FIRST_EPI) {
     // ------------------------------------------------------------- dequant
-    const int wgi = (warp - FIRST_DQ) >> 2;
-    const int wg = wgi & 1;                 // weight tile
-    const int part = wgi >> 1;              // which share of the row's chunks
-    const int c_lo = part * (C::CHUNKS / C::DQ_PARTS), c_hi = c_lo + C::CHUNKS / C::DQ_PARTS;
+    const int grp = (warp - FIRST_DQ) >> 3;        // this group takes steps it with it % DQ_GROUPS == grp
+    const int wg = ((warp - FIRST_DQ) >> 2) & 1;  // weight tile
     const int q = warp & 3;                 // TMEM lane quarter
     const int r = q * 32 + lane;            // row within the tile
     const uint32_t a_row = tmem + C::ACC_COLS + (static_cast<uint32_t>(q * 32) << 16) + wg * (KC / 2);
@@ -759,36 +812,52 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     int it = 0, rs = 0, ps = BS - AS, ra = 0;
     uint32_t rph = 0, pph = 1;
     bool ok = true;
+    XP_INIT
     for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
       const Item item = item_at(u);
       const TcPhase& P = args.ph[item.ph];
       const int sbuf = ii & 1;
+      XP(6);
       if (!mbar_wait(&sc_full[sbuf], (ii >> 1) & 1, abort_flag, 0x300)) break;
+      XP(0);
       const float* srow = ssc + sbuf * (2 * ROWS * MAX_G) + wg * (ROWS * MAX_G) + r * P.groups;
       const int spg = P.group / KC;  // K steps per scale group (0: one scale per row)
       int kbeg, kper;
       k_range(item, kbeg, kper);
       for (int kc = kbeg; kc < kbeg + kper; ++kc, ++it) {
         const int s = rs, sa = ra;
+        const int half = (kc - kbeg) % C::W_STEPS;  // K step within the weight stage
+        const bool stage_done = half == C::W_STEPS - 1 || kc == kbeg + kper - 1;
+        if (C::DQ_GROUPS > 1 && it % C::DQ_GROUPS != grp) {
+          // another group's step: only hand back our share of the weight stage
+          if (stage_done) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&wfree[s]);
+          }
+        } else {
         const float sc = FAST ? 0.f : srow[spg == 1 ? kc : spg == 0 ? 0 : kc / spg];
         const NibbleScales nsc = nibble_scales(sc);
+        XP(6);
         if (!mbar_wait(&wfull[s], rph, abort_flag, 0x310 + s)) { ok = false; break; }
-        const uint8_t* wt = sw + s * C::W_STAGE_BYTES + wg * C::W_TILE_BYTES + r * C::W_ROW_BYTES;
+        XP(1);
+        const uint8_t* wt = sw + s * C::W_STAGE_BYTES + wg * C::W_TILE_BYTES + r * C::W_LOAD_BYTES;
         const uint32_t a_stage = a_row + sa * C::A_STAGE_COLS;
         // this row's packed bytes into registers, then hand the weight slot back
         // to the producer at once; only the token tile waits for the MMA
-        constexpr int MYC = C::CHUNKS / C::DQ_PARTS;
+        constexpr int MYC = C::CHUNKS;
         uint4 v[MYC];
 #pragma unroll
         for (int ci = 0; ci < MYC; ++ci) {
-          const int c = c_lo + ci;
-          const int pc = BITS == 4 ? (c ^ ((r >> 1) & 3)) : (c ^ (r & 7));  // 64/128-byte swizzle
+          const int c = half * C::CHUNKS + ci;
+          const int pc = c ^ (r & 7);  // 128-byte swizzle
           v[ci] = *reinterpret_cast<const uint4*>(wt + pc * 16);
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&wfree[s]);
+        if (stage_done && lane == 0) mbar_arrive(&wfree[s]);
+        XP(2);
         // the TMEM A stage is free once the MMAs of step it - AS completed
         if (it >= AS && !mbar_wait(&mdone[ps], pph, abort_flag, 0x320 + sa)) { ok = false; break; }
+        XP(3);
         tc_fence_after();
         if (BITS == 4) {
 #pragma unroll
@@ -797,7 +866,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
             if (LLQ_X_NODQ) continue;
             if (FAST) codes_int4(v[ci], o);
             else dequant_int4_exact(v[ci], sc, nsc, o);
-            tc_st16(a_stage + (c_lo + ci) * 16, o);
+            tc_st16(a_stage + ci * 16, o);
           }
         } else {
 #pragma unroll
@@ -805,14 +874,17 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
             uint32_t o[16];
             dequant_int8_exact(v[ci], sc, o);
             dequant_int8_exact(v[ci + 1], sc, o + 8);
-            tc_st16(a_stage + (c_lo + ci) * 8, o);
+            tc_st16(a_stage + ci * 8, o);
           }
         }
+        XP(4);
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[wg * AS + sa]);
-        if (++rs == WS) {
+        XP(5);
+        }
+        if (stage_done && ++rs == WS) {
           rs = 0;
           rph ^= 1;
         }
@@ -825,6 +897,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
       __syncwarp();
       if (ok && lane == 0) mbar_arrive(&sc_empty[sbuf]);
     }
+    if (warp == FIRST_DQ) XP_SAVE(3);
   } else {
     // ------------------------------------------------------------- epilogue
     const int eg = (warp - FIRST_EPI) >> 2;  // token half
@@ -835,6 +908,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     constexpr int HALF = NTM / EG;
     int it = 0;
     bool ok = true;
+    XP_INIT
     for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
       const Item item = item_at(u);
       const TcPhase& P = args.ph[item.ph];
@@ -901,7 +975,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         float acc0[FAST ? HALF : 1], acc1[FAST ? HALF : 1];
 #pragma unroll
         for (int i = 0; i < (FAST ? HALF : 1); ++i) acc0[i] = acc1[i] = 0.f;
-        if (!mbar_wait_sleep(&sc_full[sbuf], (ii >> 1) & 1, abort_flag, 0x400)) break;
+        if (!mbar_wait(&sc_full[sbuf], (ii >> 1) & 1, abort_flag, 0x400)) break;
         const float* s0row = ssc + sbuf * (2 * ROWS * MAX_G) + r * P.groups;
         const float* s1row = s0row + ROWS * MAX_G;
         for (int kc = 0; kc < P.K / KC; ++kc, ++it) {
@@ -910,14 +984,15 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           tc_fence_after();
           const int gi = P.group > 0 ? (kc * KC) / P.group : 0;
           const float s0 = s0row[gi], s1 = s1row[gi];
-          const uint32_t p0 = tmem + lane_addr + pb * 2 * NTM, p1 = p0 + NTM;
+          const uint32_t p0 = tmem + lane_addr + pb * 2 * NTM + t_begin, p1 = p0 + NTM;
 #pragma unroll
           for (int c = 0; c < HALF / 8; ++c) {
-            const int t0 = t_begin + c * 8;
-            if (t0 < t_end) {
+            const int t0 = c * 8;
+            if (t_begin + t0 < t_end) {
               float v0[8], v1[8];
               tc_ld8(p0 + t0, v0);
               tc_ld8(p1 + t0, v1);
+              tc_wait_ld();  // one TMEM round trip for both tiles' columns
 #pragma unroll
               for (int i = 0; i < 8; ++i) {
                 acc0[(c * 8 + i) % (FAST ? HALF : 1)] = __fmaf_rn(s0, v0[i], acc0[(c * 8 + i) % (FAST ? HALF : 1)]);
@@ -938,32 +1013,38 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         const int ab = C::ACC_BUFS == 2 ? (ii & 1) : 0;
         const uint32_t ph = C::ACC_BUFS == 2 ? ((ii >> 1) & 1) : (ii & 1);
         const uint32_t acc_base = tmem + ab * C::ACC_BUF_COLS;
-        if (!mbar_wait_sleep(&acc_full[ab], ph, abort_flag, 0x420)) break;
+        XP(2);
+        if (!mbar_wait(&acc_full[ab], ph, abort_flag, 0x420)) break;
         tc_fence_after();
+        XP(0);
 #pragma unroll
-        for (int c = 0; c < HALF / 8; ++c) {
-          const int t0 = t_begin + c * 8;
+        for (int c = 0; c < HALF / 16; ++c) {
+          const int t0 = t_begin + c * 16;
           if (t0 < t_end) {
-            float v0[8], v1[8];
-            tc_ld8(acc_base + lane_addr + t0, v0);
-            tc_ld8(acc_base + lane_addr + SPLIT * NTM + t0, v1);
+            float v0[16], v1[16];
+            tc_ld16(acc_base + lane_addr + t0, v0);
+            tc_ld16(acc_base + lane_addr + SPLIT * NTM + t0, v1);
             if (SPLIT == 2) {
-              float w0[8], w1[8];
-              tc_ld8(acc_base + lane_addr + NTM + t0, w0);
-              tc_ld8(acc_base + lane_addr + 3 * NTM + t0, w1);
+              float w0[16], w1[16];
+              tc_ld16(acc_base + lane_addr + NTM + t0, w0);
+              tc_ld16(acc_base + lane_addr + 3 * NTM + t0, w1);
+              tc_wait_ld();
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
+              for (int i = 0; i < 16; ++i) {
                 v0[i] = __fadd_rn(v0[i], w0[i]);
                 v1[i] = __fadd_rn(v1[i], w1[i]);
               }
+            } else {
+              tc_wait_ld();
             }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) emit(c * 8 + i, v0[i], v1[i]);
+            for (int i = 0; i < 16; ++i) emit(c * 16 + i, v0[i], v1[i]);
           }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[ab]);
+        XP(1);
         if (args.fused && item.ph == 0) {
           // this warp's rows of h are stored: count it for the token tile's GEMM2 items
           __threadfence();
@@ -972,6 +1053,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         }
       }
     }
+    if (warp == FIRST_EPI) XP_SAVE(4);
   }
 
   if ((!GEMM1 || args.fused) && args.ep_on && warp >= FIRST_EPI) __threadfence_system();  // rows stored to peers
@@ -1037,10 +1119,9 @@ int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t 
 template <int BITS, int NTM>
 int phase_maps(const void* act, int64_t n_rows, int K, int E, int rows_total, const int8_t* q, CUtensorMap* tw,
                CUtensorMap* tb) {
-  constexpr int W_ROW_BYTES = KC * BITS / 8;
   const uint64_t k_bytes = static_cast<uint64_t>(K) * BITS / 8;
   int rc = make_map(tw, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, k_bytes, static_cast<uint64_t>(E) * rows_total, k_bytes,
-                    W_ROW_BYTES, ROWS, BITS == 4 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+                    128, ROWS, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   for (int i = 0; i < 4; ++i) {
     const uint32_t box = 16u << (i < 3 || NTM >= 128 ? i : 2);
@@ -1296,3 +1377,9 @@ int dense_linear_tc(const void* x, int64_t M, int K, int N, const int8_t* q, con
 }
 
 }  // namespace llq
+
+#if LLQ_X_PROF
+extern "C" int llq_x_prof_read(long long* host) {
+  return cudaMemcpyFromSymbol(host, g_xprof, sizeof(long long) * 256 * 48) == cudaSuccess ? 0 : 3;
+}
+#endif

@@ -178,6 +178,77 @@ int launch_quantize(const void* w, int64_t rows, int64_t K, int seg_len, int seg
 }
 
 // ---------------------------------------------------------------------------
+// bandwidth form of the amax path for the layout every checkpoint uses: bf16
+// weights, 128-element groups that divide the row.  A group is 256 bytes, so a
+// half-warp covers it with one 16-byte load per lane; the amax is a 4-step
+// shuffle over the half-warp, and each lane writes its 8 codes as one 4-byte
+// (packed INT4) or 8-byte (INT8) store -- the group's 64 or 128 output bytes
+// leave as one contiguous half-warp store.  Same arithmetic as above: the exact
+// bf16 amax, IEEE division by Qmax, rint of the IEEE quotient, clamp.
+// ---------------------------------------------------------------------------
+constexpr int kG128Unroll = 2;  // groups per half-warp per iteration (loads in flight)
+
+template <bool PACK4>
+__global__ void __launch_bounds__(256) quantize_g128_bf16_kernel(const uint4* __restrict__ w, int64_t ngroups,
+                                                                 int bits, int scale_round,
+                                                                 int8_t* __restrict__ q,
+                                                                 float* __restrict__ scale_out) {
+  const int lane = threadIdx.x & 31;
+  const int sub = lane & 15;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const float qmax = static_cast<float>((1 << (bits - 1)) - 1);
+  const float qmin = -qmax - 1.f;
+  // each warp iteration covers 2 * kG128Unroll groups; the loop is warp-uniform so that
+  // the half-warp shuffles always see a converged warp
+  for (int64_t base = warp * 2 * kG128Unroll; base < ngroups; base += nwarps * 2 * kG128Unroll) {
+    uint4 v[kG128Unroll];
+#pragma unroll
+    for (int u = 0; u < kG128Unroll; ++u) {
+      const int64_t g = base + 2 * u + (lane >> 4);
+      v[u] = g < ngroups ? __ldcs(w + g * 16 + sub) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kG128Unroll; ++u) {
+      const int64_t g = base + 2 * u + (lane >> 4);
+      const uint32_t wd[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      float x[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        x[2 * i] = __uint_as_float(wd[i] << 16);
+        x[2 * i + 1] = __uint_as_float(wd[i] & 0xFFFF0000u);
+      }
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(x[i]));
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float sc = apply_scale_round(__fdiv_rn(amax, qmax), scale_round);
+      const float safe = sc > 0.f ? sc : 1.f;
+      if (g >= ngroups) continue;
+      if (sub == 0) scale_out[g] = sc;
+      int c[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) c[i] = static_cast<int>(quant_code(x[i], safe, qmin, qmax));
+      if (PACK4) {
+        uint32_t b = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) b |= static_cast<uint32_t>(c[i] & 0xF) << (4 * i);
+        reinterpret_cast<uint32_t*>(q)[g * 16 + sub] = b;
+      } else {
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          lo |= static_cast<uint32_t>(c[i] & 0xFF) << (8 * i);
+          hi |= static_cast<uint32_t>(c[i + 4] & 0xFF) << (8 * i);
+        }
+        reinterpret_cast<uint2*>(q)[g * 16 + sub] = make_uint2(lo, hi);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // dequantize: 8 consecutive elements of one row per thread
 // ---------------------------------------------------------------------------
 template <typename OutT>
@@ -211,6 +282,45 @@ __global__ void dequantize_kernel(const int8_t* __restrict__ q, const float* __r
       const float s = scale[row * groups + (group > 0 ? k / group : 0)];
       out[e] = from_f32<OutT>(__fmul_rn(static_cast<float>(v), s));
     }
+  }
+}
+
+// bf16 output, 16 elements (one scale) per thread: an 8-byte (INT4) or 16-byte
+// (INT8) load, 32 bytes stored as two 16-byte stores; the row and scale index come
+// from one 32-bit division per 16 elements.  Requires K % 16 == 0 and a group that
+// is a multiple of 16 (or one scale per row).
+template <bool INT4>
+__global__ void __launch_bounds__(256) dequantize16_bf16_kernel(const int8_t* __restrict__ q,
+                                                                const float* __restrict__ scale,
+                                                                int64_t chunks, uint32_t chunks_per_row,
+                                                                uint32_t chunks_per_group, int groups,
+                                                                uint4* __restrict__ out) {
+  for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < chunks;
+       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = c / chunks_per_row;
+    const uint32_t cr = static_cast<uint32_t>(c - row * chunks_per_row);
+    const float s = __ldg(scale + row * groups + cr / chunks_per_group);
+    int v[16];
+    if (INT4) {
+      const uint2 b = __ldcs(reinterpret_cast<const uint2*>(q) + c);
+      const uint32_t w[2] = {b.x, b.y};
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = static_cast<int>(w[i >> 3] << (28 - 4 * (i & 7))) >> 28;
+    } else {
+      const uint4 b = __ldcs(reinterpret_cast<const uint4*>(q) + c);
+      const uint32_t w[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = static_cast<int>(w[i >> 2] << (24 - 8 * (i & 3))) >> 24;
+    }
+    uint32_t o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      __nv_bfloat162 p = __floats2bfloat162_rn(__fmul_rn(static_cast<float>(v[2 * i]), s),
+                                               __fmul_rn(static_cast<float>(v[2 * i + 1]), s));
+      o[i] = *reinterpret_cast<uint32_t*>(&p);
+    }
+    __stcs(out + 2 * c, make_uint4(o[0], o[1], o[2], o[3]));
+    __stcs(out + 2 * c + 1, make_uint4(o[4], o[5], o[6], o[7]));
   }
 }
 
@@ -271,6 +381,21 @@ int quantize_impl(const void* w, int w_dtype, int64_t rows, int64_t K, int bits,
   int seg_len = 0, spr = 0;
   int rc = segments(K, group_size, &seg_len, &spr);
   if (rc) return rc;
+  const bool aligned = (reinterpret_cast<uintptr_t>(w) & 15) == 0 && (reinterpret_cast<uintptr_t>(q) & 7) == 0;
+  if (w_dtype == LLQ_BF16 && seg_len == 128 && search == LLQ_SEARCH_AMAX && errors == nullptr && aligned) {
+    const int64_t ngroups = rows * spr;
+    const int threads = 256;
+    const int64_t need = (ngroups + 2 * kG128Unroll - 1) / (2 * kG128Unroll) * 32;
+    const int64_t want = (need + threads - 1) / threads;
+    const unsigned blocks = static_cast<unsigned>(want < num_sms() * 8 ? want : num_sms() * 8);
+    if (bits == 4 && pack)
+      quantize_g128_bf16_kernel<true><<<blocks, threads, 0, st>>>(static_cast<const uint4*>(w), ngroups, bits,
+                                                                  scale_round, q, scale);
+    else
+      quantize_g128_bf16_kernel<false><<<blocks, threads, 0, st>>>(static_cast<const uint4*>(w), ngroups, bits,
+                                                                   scale_round, q, scale);
+    return check_launch("quantize_g128_bf16_kernel");
+  }
   switch (w_dtype) {
     case LLQ_F32:
       return launch_quantize<float>(w, rows, K, seg_len, spr, bits, search, grid, max_shrink,
@@ -294,6 +419,23 @@ int dequantize_impl(const int8_t* q, const float* scale, int64_t rows, int64_t K
   const bool grouped = !(group_size == -1 || group_size <= 0 || K % group_size != 0);
   const int group = grouped ? group_size : 0;
   const int groups = grouped ? static_cast<int>(K / group_size) : 1;
+  const bool vec_ok = out_dtype == LLQ_BF16 && K % 16 == 0 && (!grouped || group % 16 == 0) &&
+                      (bits == 8 ? !packed : packed != 0) && K / 16 <= 0x7fffffff &&
+                      (reinterpret_cast<uintptr_t>(q) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+  if (vec_ok) {
+    const int64_t chunks = rows * K / 16;
+    const uint32_t cpr = static_cast<uint32_t>(K / 16);
+    const uint32_t cpg = grouped ? static_cast<uint32_t>(group / 16) : cpr;
+    const int64_t want = (chunks + 255) / 256;
+    const unsigned blocks = static_cast<unsigned>(want < num_sms() * 8 ? want : num_sms() * 8);
+    if (bits == 4)
+      dequantize16_bf16_kernel<true><<<blocks, 256, 0, st>>>(q, scale, chunks, cpr, cpg, groups,
+                                                             static_cast<uint4*>(out));
+    else
+      dequantize16_bf16_kernel<false><<<blocks, 256, 0, st>>>(q, scale, chunks, cpr, cpg, groups,
+                                                              static_cast<uint4*>(out));
+    return check_launch("dequantize16_bf16_kernel");
+  }
   const int64_t work = (rows * K + 7) / 8;
   const int threads = 256;
   const int64_t want = (work + threads - 1) / threads;

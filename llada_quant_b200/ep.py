@@ -43,6 +43,14 @@ import torch.distributed as dist
 LocalFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
 
 
+def _mark(marks: Optional[list], name: str) -> None:
+    """Record a CUDA event named ``name`` on the current stream into ``marks`` (phase timing)."""
+    if marks is not None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        marks.append((name, ev))
+
+
 def _exchange(t: torch.Tensor, out_splits, in_splits, group) -> torch.Tensor:
     out = t.new_empty((sum(out_splits),) + tuple(t.shape[1:]))
     dist.all_to_all_single(out, t.contiguous(), output_split_sizes=list(out_splits),
@@ -51,14 +59,15 @@ def _exchange(t: torch.Tensor, out_splits, in_splits, group) -> torch.Tensor:
 
 
 def ep_dispatch_combine(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor,
-                        experts_per_rank: int, local_fn: LocalFn, group=None) -> torch.Tensor:
+                        experts_per_rank: int, local_fn: LocalFn, group=None,
+                        marks: Optional[list] = None) -> torch.Tensor:
     """Steps 2-5 above.  ``local_fn(rows, local_expert_ids, routed_w) -> rows`` computes
     ``routed_w * expert(row)`` (bf16) for each received row."""
     world = dist.get_world_size(group)
     T, H = x.shape
     k = topk_ids.shape[1]
     if x.is_cuda:
-        return _ep_cuda(x, topk_w, topk_ids, experts_per_rank, local_fn, group, world)
+        return _ep_cuda(x, topk_w, topk_ids, experts_per_rank, local_fn, group, world, marks)
     ids = topk_ids.reshape(-1).to(torch.int64)
     dest = torch.div(ids, experts_per_rank, rounding_mode="floor")
     order = torch.argsort(dest, stable=True)                     # sorted (token, slot) entries
@@ -87,7 +96,7 @@ def ep_dispatch_combine(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.T
     return acc.to(x.dtype)
 
 
-def _ep_cuda(x, topk_w, topk_ids, experts_per_rank, local_fn, group, world):
+def _ep_cuda(x, topk_w, topk_ids, experts_per_rank, local_fn, group, world, marks=None):
     """The same steps on the package's kernels (called below the dispatcher): grouping over
     ranks (moe_align), one pack kernel for rows + metadata, two NCCL all-to-alls out and one
     back, the local layer, one combine kernel.  The single host synchronisation reads the
@@ -101,18 +110,25 @@ def _ep_cuda(x, topk_w, topk_ids, experts_per_rank, local_fn, group, world):
     rows, lid, wts, inv = ops._ep_pack_impl(x, ids32, topk_w, order, experts_per_rank)
     meta = torch.stack([lid, wts.view(torch.int32)], dim=1)
     send_counts = (offsets[1:] - offsets[:-1]).to(torch.int64)
+    _mark(marks, "pack")
     recv_counts = torch.empty_like(send_counts)
     dist.all_to_all_single(recv_counts, send_counts, group=group)
     counts = torch.stack([send_counts, recv_counts]).tolist()
     sc, rc = counts[0], counts[1]
+    _mark(marks, "counts")
     recv_rows = _exchange(rows, rc, sc, group)
     recv_meta = _exchange(meta, rc, sc, group)
+    _mark(marks, "dispatch")
     if recv_rows.shape[0]:
         y = local_fn(recv_rows, recv_meta[:, 0:1], recv_meta[:, 1:2].view(torch.float32))
     else:
         y = recv_rows.new_empty((0, H))
+    _mark(marks, "experts")
     back = _exchange(y, sc, rc, group)
-    return ops._ep_combine_impl(back, inv, k)
+    _mark(marks, "return")
+    out = ops._ep_combine_impl(back, inv, k)
+    _mark(marks, "combine")
+    return out
 
 
 def local_packed_fn(packed, impl: int) -> LocalFn:
@@ -127,15 +143,20 @@ def local_packed_fn(packed, impl: int) -> LocalFn:
 
 def ep_moe_layer(x: torch.Tensor, gate_w: torch.Tensor, packed, top_k: int, rank: int, world: int,
                  bias: Optional[torch.Tensor] = None, renormalize: bool = False, impl: int = 0,
-                 group=None, window: Optional["EPWindow"] = None) -> torch.Tensor:
+                 group=None, window: Optional["EPWindow"] = None,
+                 marks: Optional[list] = None) -> torch.Tensor:
     """One expert-parallel MoE layer on this rank's tokens ``x`` [T_r, H]: over the
-    peer-memory ``window`` when one is given, else over torch.distributed all-to-alls."""
+    peer-memory ``window`` when one is given, else over torch.distributed all-to-alls.
+    ``marks``, when given, collects (phase name, CUDA event) pairs recorded at the end of
+    each phase on the current stream."""
     from . import ops
+    _mark(marks, "start")
     topk_w, topk_ids, _ = ops._route_impl(x, gate_w, top_k, bias, renormalize)
+    _mark(marks, "route")
     if window is not None:
-        return window.layer(x, topk_w, topk_ids, packed, impl)
+        return window.layer(x, topk_w, topk_ids, packed, impl, marks=marks)
     return ep_dispatch_combine(x, topk_w, topk_ids, packed.num_experts, local_packed_fn(packed, impl),
-                               group=group)
+                               group=group, marks=marks)
 
 
 class EPWindow:
@@ -188,7 +209,8 @@ class EPWindow:
             self._ws = torch.empty(n, dtype=torch.uint8, device=self.device)
         return self._ws
 
-    def layer(self, x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor, packed, impl: int) -> torch.Tensor:
+    def layer(self, x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor, packed, impl: int,
+              marks: Optional[list] = None) -> torch.Tensor:
         """Steps 2-5 for routed tokens ``x`` [T, H] against this rank's expert shard ``packed``."""
         from ._lib import check, load
         from .ops import _group_of, _stream
@@ -208,15 +230,18 @@ class EPWindow:
         check(lib.llq_ep_dispatch(x.data_ptr(), ids.data_ptr(), w.data_ptr(), T, k, H, E_local, self.base,
                                   self.peers.data_ptr(), self.rank, self.world, self.cap, self.epoch,
                                   inv.data_ptr(), st), "ep_dispatch")
+        _mark(marks, "dispatch")
         ws = self._workspace(E_local, I)
         check(lib.llq_ep_experts(self.base, self.peers.data_ptr(), self.rank, self.world, self.cap, self.epoch,
                                  packed.qw1.data_ptr(), packed.sw1.data_ptr(), packed.qw2.data_ptr(),
                                  packed.sw2.data_ptr(), E_local, H, I, packed.bits,
                                  _group_of(packed.qw1, packed.sw1, packed.bits), T * k, ws.data_ptr(),
                                  ws.numel(), impl, st), "ep_experts")
+        _mark(marks, "experts")
         out = torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
         check(lib.llq_ep_combine_wait(self.base, self.rank, self.world, self.cap, self.epoch, inv.data_ptr(),
                                       T, k, H, out.data_ptr(), st), "ep_combine")
+        _mark(marks, "combine")
         return out
 
     def close(self) -> None:

@@ -74,13 +74,17 @@ def fused_moe(hidden_states: torch.Tensor, w1, w2, gating_output: Optional[torch
 
 def moe_layer(x: torch.Tensor, gate_w: torch.Tensor, packed: PackedExperts, top_k: int,
               bias: Optional[torch.Tensor] = None, renormalize: bool = False,
-              impl: str = "auto", recorder=None) -> torch.Tensor:
+              impl: str = "auto", recorder=None, capture=None, name: str = "") -> torch.Tensor:
     """Router + routed experts, the forward of a PACKED LLaDA MoE block: one router
     kernel (bf16 logits, fp32 softmax, top-k) then :func:`fused_moe`.  With a
     ``routing_stats.RoutingRecorder`` the call's per-expert loads are added to it on
-    the device, from the expert offsets the GEMMs used."""
+    the device, from the expert offsets the GEMMs used; with a
+    ``router_capture.RouterCapture`` the router kernel's own ids and logits are
+    recorded under ``name``."""
     # eager hot path: the op implementations directly (no per-call dispatcher cost)
-    topk_w, topk_ids, _ = ops._route_impl(x, gate_w, top_k, bias, renormalize)
+    topk_w, topk_ids, logits = ops._route_impl(x, gate_w, top_k, bias, renormalize)
+    if capture is not None:
+        capture.record(name, topk_ids, logits)
     out = ops._fused_moe_packed_impl(x, packed.qw1, packed.sw1, packed.qw2, packed.sw2, topk_w,
                                      topk_ids, packed.bits, IMPL[impl])
     if recorder is not None:

@@ -83,20 +83,19 @@ class QuantLinear(nn.Module):
         return out
 
     def dequantize_weight(self) -> torch.Tensor:
+        """The weight as a dense ``compute_dtype`` matrix (one dequantize kernel launch)."""
         return dequantize_tensor(self.qweight, self.scale, self.bits, self.group_size,
                                  dtype=self.compute_dtype, packed=self.packed)
 
     def storage_bytes(self) -> int:
-        """Resident bytes of this module's weight representation."""
-        total = self.qweight.numel() * self.qweight.element_size()
-        total += self.scale.numel() * self.scale.element_size()
-        if self.bias is not None:
-            total += self.bias.numel() * self.bias.element_size()
-        return total
+        """Bytes held on the device by qweight, scale and (if any) bias."""
+        tensors = [self.qweight, self.scale] + ([self.bias] if self.bias is not None else [])
+        return sum(t.numel() * t.element_size() for t in tensors)
 
     def extra_repr(self) -> str:
-        return (f"in_features={self.in_features}, out_features={self.out_features}, "
-                f"bits={self.bits}, group_size={self.group_size}, packed={self.packed}")
+        layout = "int4x2" if self.packed else f"int{self.bits}"
+        return (f"{self.in_features} -> {self.out_features}, {layout} codes, "
+                f"group {self.group_size}, B200 kernel {'on' if self.uses_kernel() else 'off'}")
 
     def uses_kernel(self) -> bool:
         return (self.compute_dtype == torch.bfloat16 and self.scale.dtype == torch.float32

@@ -15,6 +15,8 @@ generated ``PackedQuant<Cls>`` subclass as ``src/LLaDA_Quant/runtime/moe.py``
 
 from __future__ import annotations
 
+import functools
+
 from dataclasses import dataclass
 from typing import Dict, Tuple
 
@@ -115,7 +117,8 @@ def _meta(self: nn.Module) -> dict:
 
 
 def _packed_expert_weight(self: nn.Module, which: str) -> torch.Tensor:
-    """runtime/moe.py:199-216, one dequantize kernel per access (fresh tensor each time)."""
+    """Dense ``compute_dtype`` w1 or w2, made by one dequantize kernel launch on every access
+    (so each access returns a new tensor, as the PACKED property of runtime/moe.py:199-216)."""
     meta = _meta(self)
     suffix = which[-1]
     return dequantize_tensor(getattr(self, f"_qw{suffix}"), getattr(self, f"_sw{suffix}"),
@@ -146,52 +149,45 @@ def _blocked_method(name: str):
     return blocked
 
 
-_PACKED_CLASS_CACHE: Dict[type, type] = {}
-
-
-def _packed_class(cls: type) -> type:
-    """runtime/moe.py:246-269, plus the ``packed_experts`` handle."""
-    if getattr(cls, "_llada_quant_packed", False):
-        return cls
-    cached = _PACKED_CLASS_CACHE.get(cls)
-    if cached is not None:
-        return cached
-    namespace = {
+@functools.lru_cache(maxsize=None)
+def _packed_subclass(cls: type) -> type:
+    """Build (once per block class) the ``PackedQuant<Cls>`` subclass whose ``w1``/``w2``
+    are read-only properties over the packed buffers (the reference's generated class,
+    runtime/moe.py:246-269 -- name and behaviour are part of its checkpoint contract),
+    with the in-place loaders refused and a ``packed_experts()`` handle added."""
+    attrs = {
         "_llada_quant_packed": True,
         "_packed_expert_weight": _packed_expert_weight,
         "packed_experts": _packed_experts,
-        W1: property(lambda self: self._packed_expert_weight(W1)),
-        W2: property(lambda self: self._packed_expert_weight(W2)),
         "__doc__": f"{cls.__name__} with w1/w2 served from packed integer buffers.",
     }
-    for method in WEIGHT_MUTATING_METHODS:
-        if hasattr(cls, method):
-            namespace[method] = _blocked_method(method)
-    generated = type(f"PackedQuant{cls.__name__}", (cls,), namespace)
-    _PACKED_CLASS_CACHE[cls] = generated
-    return generated
+    attrs.update({w: property(functools.partial(_packed_expert_weight, which=w)) for w in (W1, W2)})
+    attrs.update({m: _blocked_method(m) for m in WEIGHT_MUTATING_METHODS if hasattr(cls, m)})
+    return type(f"PackedQuant{cls.__name__}", (cls,), attrs)
+
+
+def _packed_class(cls: type) -> type:
+    """The packed subclass of ``cls`` (``cls`` itself when it already is one)."""
+    return cls if getattr(cls, "_llada_quant_packed", False) else _packed_subclass(cls)
 
 
 def install_packed_expert_access(block: nn.Module) -> None:
-    """runtime/moe.py:272-286."""
-    missing = [name for name in PACKED_BUFFERS if not hasattr(block, name)]
-    if missing:
-        raise RuntimeError(f"cannot install packed access, missing buffers: {missing}")
-    for name in EXPERT_PARAM_NAMES:
-        block._parameters.pop(name, None)
+    """Switch ``block`` to packed serving in place: drop its dense expert parameters and
+    re-class it (runtime/moe.py:272-286); the packed buffers must already be attached."""
+    absent = [n for n in PACKED_BUFFERS if not hasattr(block, n)]
+    if absent:
+        raise RuntimeError(f"cannot install packed access, missing buffers: {absent}")
+    for n in EXPERT_PARAM_NAMES:
+        block._parameters.pop(n, None)
     block.__class__ = _packed_class(type(block))
 
 
 def is_packed_expert_block(module: nn.Module) -> bool:
-    """runtime/moe.py:289-291."""
-    return getattr(type(module), "_llada_quant_packed", False)
+    """True for blocks re-classed by :func:`install_packed_expert_access` (runtime/moe.py:289-291)."""
+    return bool(getattr(type(module), "_llada_quant_packed", False))
 
 
 def expert_storage_bytes(block: nn.Module) -> int:
-    """runtime/moe.py:294-301."""
-    total = 0
-    for name in PACKED_BUFFERS:
-        buf = getattr(block, name, None)
-        if buf is not None:
-            total += buf.numel() * buf.element_size()
-    return total
+    """Device bytes of the block's packed expert buffers, codes and scales (runtime/moe.py:294-301)."""
+    bufs = (getattr(block, n, None) for n in PACKED_BUFFERS)
+    return sum(b.numel() * b.element_size() for b in bufs if b is not None)

@@ -20,7 +20,8 @@ from . import ops
 
 @dataclass
 class ExpertTokenStats:
-    """Measured routing load, from real ``topk_ids`` (moe_regime.py:150-194)."""
+    """Per-expert row counts of real routing, with the summary fields and ``to_dict`` keys
+    of the reference report (analysis/moe_regime.py:150-194)."""
 
     tokens: int
     top_k: int
@@ -29,38 +30,35 @@ class ExpertTokenStats:
 
     @property
     def active_experts(self) -> int:
-        return sum(1 for c in self.counts if c > 0)
+        """Experts that received at least one row."""
+        return sum(c > 0 for c in self.counts)
 
     @property
     def mean(self) -> float:
-        return sum(self.counts) / len(self.counts) if self.counts else 0.0
+        return float(sum(self.counts)) / len(self.counts) if self.counts else 0.0
 
     @property
     def imbalance(self) -> float:
-        """Max load over mean load. 1.0 is perfect balance; the max sets step time."""
-        return max(self.counts) / self.mean if self.counts and self.mean else 1.0
+        """Busiest expert's rows divided by the mean; the busiest expert bounds a layer's
+        time, so 1.0 means no expert waits on another."""
+        m = self.mean
+        return max(self.counts) / m if self.counts and m else 1.0
 
     def percentile(self, p: float) -> float:
+        """Nearest-rank percentile of the counts (index rounded on the sorted list)."""
         if not self.counts:
             return 0.0
-        ordered = sorted(self.counts)
-        idx = min(len(ordered) - 1, max(0, int(round(p / 100 * (len(ordered) - 1)))))
-        return float(ordered[idx])
+        s = sorted(self.counts)
+        i = int(round(p / 100.0 * (len(s) - 1)))
+        return float(s[min(max(i, 0), len(s) - 1)])
 
     def to_dict(self) -> dict:
-        return {
-            "tokens": self.tokens,
-            "top_k": self.top_k,
-            "num_experts": self.num_experts,
-            "active_experts": self.active_experts,
-            "min": min(self.counts) if self.counts else 0,
-            "p50": self.percentile(50),
-            "mean": round(self.mean, 2),
-            "p90": self.percentile(90),
-            "p99": self.percentile(99),
-            "max": max(self.counts) if self.counts else 0,
-            "imbalance_max_over_mean": round(self.imbalance, 3),
-        }
+        c = self.counts
+        return {"tokens": self.tokens, "top_k": self.top_k, "num_experts": self.num_experts,
+                "active_experts": self.active_experts, "min": min(c) if c else 0,
+                "p50": self.percentile(50), "mean": round(self.mean, 2), "p90": self.percentile(90),
+                "p99": self.percentile(99), "max": max(c) if c else 0,
+                "imbalance_max_over_mean": round(self.imbalance, 3)}
 
 
 def expert_counts(topk_ids: torch.Tensor, num_experts: int) -> torch.Tensor:

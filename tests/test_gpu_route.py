@@ -137,3 +137,36 @@ def test_ep_pack_and_combine_exact():
     for j in range(k):
         ref = (ref + b[to_np(inv).reshape(T, k)[:, j]]).astype(np.float32)
     assert np.array_equal(to_np(out), S.round_to_bf16(ref))
+
+
+def test_router_capture_records_the_kernels_routing():
+    """RouterCapture (trajectory/llada.py:157-268 accessors) fed by moe_layer's own router:
+    the recorded ids are those the layer's GEMMs used, the logits those of the oracle."""
+    from llada_quant_b200 import symmetric as G
+    from llada_quant_b200.fused_moe import moe_layer
+    from llada_quant_b200.moe import PackedExperts
+    from llada_quant_b200.router_capture import RouterCapture
+    from tests._util import synthetic_layer, synthetic_tokens
+    T, E, H, I, k = 64, 16, 1024, 512, 2
+    w1, w2 = synthetic_layer(E, H, I, seed=4)
+    r1 = G.quantize_tensor(w1.cuda(), bits=4, group_size=128)
+    r2 = G.quantize_tensor(w2.cuda(), bits=4, group_size=128)
+    packed = PackedExperts(r1.q, r1.scale, r2.q, r2.scale, 4, 128)
+    gw = (torch.randn(E, H, generator=torch.Generator().manual_seed(5)) * 0.02).to(torch.bfloat16)
+    with RouterCapture() as cap:
+        for layer in range(2):
+            x = synthetic_tokens(T, H, seed=20 + layer).cuda()
+            moe_layer(x, gw.cuda(), packed, k, capture=cap, name=f"layers.{layer}.mlp")
+            ref_logits = M.router_logits(to_np(x), to_np(gw))
+            got = cap.gates[f"layers.{layer}.mlp"].numpy()
+            ulps = np.abs(S.bf16_bits(got).astype(np.int32) - S.bf16_bits(ref_logits).astype(np.int32))
+            assert ulps.max() <= 1
+            ids = cap.topk_ids[f"layers.{layer}.mlp"]
+            assert ids.dtype == torch.int64 and tuple(ids.shape) == (T, k)
+            ref_w, ref_ids = M.route_topk(got, k)
+            _check_topk(ref_w, ids.numpy(), ref_w, ref_ids, M.softmax_fp32(got))
+    assert cap.layer_names == ["layers.0.mlp", "layers.1.mlp"]
+    moe_layer(x, gw.cuda(), packed, k, capture=cap, name="after")  # removed: nothing recorded
+    assert "after" not in cap.layer_names
+    cap.clear()
+    assert cap.layer_names == []

@@ -76,7 +76,7 @@ def test_quant_linear_buffers_and_storage():
     assert tuple(m.qweight.shape) == (512, 512) and m.qweight.dtype == torch.int8
     assert tuple(m.scale.shape) == (512, 8) and m.scale.dtype == torch.float32
     assert m.storage_bytes() == 512 * 512 + 512 * 8 * 4 + 512 * 2
-    assert "packed=True" in m.extra_repr()
+    assert "int4x2 codes" in m.extra_repr()
     m8 = QuantLinear(100, 256, bits=8, group_size=128)
     assert tuple(m8.scale.shape) == (256, 1)  # per-row fallback when the group does not divide K
     assert kernel_supports(1024, 512, 128) and kernel_supports(2048, 256, -1)
@@ -86,3 +86,21 @@ def test_quant_linear_buffers_and_storage():
         QuantLinear(64, 64, bits=3)
     with pytest.raises(RuntimeError, match="CUDA"):
         m(torch.zeros(2, 1024))
+
+
+def test_router_capture_accessors_on_host_tensors():
+    import torch
+    from llada_quant_b200.router_capture import RouterCapture
+    cap = RouterCapture()
+    cap.record("b", torch.tensor([[1, 0]], dtype=torch.int32), torch.zeros(1, 4, dtype=torch.bfloat16))
+    cap.record("a", torch.tensor([[2, 3]], dtype=torch.int32), torch.ones(1, 4, dtype=torch.bfloat16))
+    assert cap.layer_names == ["a", "b"]
+    assert cap.topk_ids["a"].dtype == torch.int64 and cap.topk_ids["a"].tolist() == [[2, 3]]
+    assert cap.gates["a"].dtype == torch.float32
+    with cap:
+        pass
+    cap.record("c", torch.zeros(1, 2, dtype=torch.int32), torch.zeros(1, 4))
+    assert "c" not in cap.layer_names
+    cap.remove()
+    cap.clear()
+    assert cap.layer_names == []
