@@ -372,7 +372,9 @@ def _ref_layer(x, gate_w, layer, grouped: bool, deq):
     gt, up = a[:, :I].float(), a[:, I:].float()
     h = ((gt / (1.0 + torch.exp(-gt))).to(torch.bfloat16).float() * up).to(torch.bfloat16)
     if grouped:
-        y = torch._grouped_mm(h, W2.transpose(1, 2), offs=offs, out_dtype=torch.float32)
+        # the grouped GEMM only returns its input dtype: the bf16 result is widened before the
+        # routed-weight multiply (one extra bf16 rounding of the expert output)
+        y = torch._grouped_mm(h, W2.transpose(1, 2), offs=offs).float()
     else:
         y = torch.empty(h.shape[0], H, dtype=torch.float32, device=x.device)
         o = 0

@@ -44,8 +44,14 @@ struct MoeWorkspace {
   void* y_slots;
   int32_t* tile_done;
   int tile_done_n;
+  void* w1_bf16;  // prefill-sized calls: the layer's weights dequantized once (else null)
+  void* w2_bf16;
   size_t total;
 };
+
+// prefill-sized call: enough routed rows per expert that every weight meets many
+// token tiles, so dequantizing the weights once and running bf16 GEMMs is cheaper
+bool prefill_call(int64_t T, int k, int E) { return T * k >= static_cast<int64_t>(E) * kPrefillRowsPerExpert; }
 
 MoeWorkspace carve(void* base, int64_t T, int k, int E, int H, int I) {
   MoeWorkspace w{};
@@ -65,6 +71,11 @@ MoeWorkspace carve(void* base, int64_t T, int k, int E, int H, int I) {
   w.y_slots = take(static_cast<size_t>(n) * H * 2 + 4096);
   w.tile_done_n = gemm12_counter_slots(n, E);
   w.tile_done = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * w.tile_done_n));
+  w.w1_bf16 = w.w2_bf16 = nullptr;
+  if (prefill_call(T, k, E)) {
+    w.w1_bf16 = take(static_cast<size_t>(E) * 2 * I * H * 2);
+    w.w2_bf16 = take(static_cast<size_t>(E) * H * I * 2);
+  }
   w.total = off;
   return w;
 }
@@ -256,6 +267,20 @@ int llq_fused_moe_packed(const void* x, const int8_t* qw1, const float* sw1, con
   }
   rc = permute_impl(x, T, H, k, ws.sorted_slots, ws.x_sorted, st, 0);
   if (rc) return rc;
+  if (ws.w1_bf16 != nullptr && pick_impl(impl, E, I, H, bits, group_size, true) == LLQ_GEMM_TCGEN05 &&
+      pick_impl(impl, E, H, I, bits, group_size, false) == LLQ_GEMM_TCGEN05) {
+    // the weights are bit-identical to dequantize_tensor's, so are the products
+    rc = dequantize_impl(qw1, sw1, static_cast<int64_t>(E) * 2 * I, H, bits, group_size, bits == 4, ws.w1_bf16,
+                         LLQ_BF16, st);
+    if (rc) return rc;
+    rc = dequantize_impl(qw2, sw2, static_cast<int64_t>(E) * H, I, bits, group_size, bits == 4, ws.w2_bf16,
+                         LLQ_BF16, st);
+    if (rc) return rc;
+    rc = gemm12_fused_bf16_tc(ws.x_sorted, ws.offsets, ws.sorted_slots, topk_w, n, E, H, I, ws.w1_bf16, ws.w2_bf16,
+                              ws.h_sorted, ws.y_slots, ws.tile_done, st);
+    if (rc) return rc;
+    return combine_impl(ws.y_slots, T, k, H, out, st);
+  }
   if (pick_impl(impl, E, I, H, bits, group_size, true) == LLQ_GEMM_TCGEN05 &&
       pick_impl(impl, E, H, I, bits, group_size, false) == LLQ_GEMM_TCGEN05) {
     rc = gemm12_fused_tc(ws.x_sorted, ws.offsets, ws.sorted_slots, topk_w, n, E, H, I, qw1, sw1, qw2, sw2, bits,

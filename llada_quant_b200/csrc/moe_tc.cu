@@ -83,20 +83,23 @@ constexpr long long kTimeoutCycles = 4000000000LL;
 
 template <bool GEMM1, int BITS, bool FAST, int NTM>
 struct Cfg {
+  // BITS == 16: the weights are already bf16 (dequantized once per layer call for
+  // prefill-sized batches) and reach the tensor cores from shared memory by TMA
+  static constexpr bool SS = BITS == 16;
   static constexpr int W_ROW_BYTES = KC * BITS / 8;  // packed bytes of one row per K step
   // a weight load brings 128 bytes of each row (two K steps at INT4): twice the
   // DRAM burst of one step, half the TMA row requests per weight byte
-  static constexpr int W_STEPS = 128 / W_ROW_BYTES;
+  static constexpr int W_STEPS = SS ? 1 : 128 / W_ROW_BYTES;
   static constexpr int W_LOAD_BYTES = W_ROW_BYTES * W_STEPS;
   static constexpr int W_TILE_BYTES = ROWS * W_LOAD_BYTES;
   static constexpr int W_STAGE_BYTES = 2 * W_TILE_BYTES;
   static constexpr int B_STAGE_BYTES = NTM * KC * 2;
-  static constexpr int SCALE_BUF_BYTES = 2 * ROWS * MAX_G * 4;
+  static constexpr int SCALE_BUF_BYTES = SS ? 0 : 2 * ROWS * MAX_G * 4;
   // Two rings: packed weights, released as soon as the dequantizing warps have
   // copied them to registers, and token tiles, released when the step's MMAs
   // complete.  Weight slots thus turn over at the speed of HBM, independently
   // of the MMA pipeline, and the weight ring takes what shared memory is left.
-  static constexpr int B_STAGES = 3;
+  static constexpr int B_STAGES = SS ? 2 : 3;
   static constexpr int W_STAGES_FIT =
       (220 * 1024 - 2 * SCALE_BUF_BYTES - B_STAGES * B_STAGE_BYTES) / W_STAGE_BYTES;
   static constexpr int W_STAGES = W_STAGES_FIT > 8 ? 8 : W_STAGES_FIT;
@@ -115,7 +118,7 @@ struct Cfg {
   // dequantizing warps: DQ_GROUPS groups of 8 (one warpgroup per weight tile)
   // that take alternate K steps, so that one group's waits overlap the other's math
   static constexpr int DQ_GROUPS = FAST ? 1 : LLQ_X_DQG;
-  static constexpr int DQ_WARPS = 8 * DQ_GROUPS;
+  static constexpr int DQ_WARPS = SS ? 0 : 8 * DQ_GROUPS;
   static constexpr int EPI_WARPS = LLQ_X_EPW;  // token groups of one warpgroup each
   static constexpr int FIRST_MMA = 2;  // warp 0 loads weights and scales, warp 1 token tiles
   static constexpr int FIRST_DQ = FIRST_MMA + MMA_WARPS;
@@ -124,11 +127,11 @@ struct Cfg {
   // exact mode: the accumulators are double-buffered across items when they
   // fit beside two A stages, so that an item's epilogue overlaps the next
   // item's MMAs (64-token tiles); 128-token tiles keep one buffer
-  static constexpr int ACC_BUFS = (!FAST && 2 * 2 * SPLIT * NTM <= 256) ? 2 : 1;
+  static constexpr int ACC_BUFS = (!FAST && 2 * 2 * SPLIT * NTM <= (SS ? 512 : 256)) ? 2 : 1;
   static constexpr int ACC_BUF_COLS = 2 * SPLIT * NTM;
   static constexpr int ACC_COLS = FAST ? 4 * NTM : ACC_BUFS * ACC_BUF_COLS;
   static constexpr int A_STAGE_COLS = KC;  // 64 columns per tile
-  static constexpr int A_STAGES_FIT = static_cast<int>(TMEM_COLS - ACC_COLS) / A_STAGE_COLS;
+  static constexpr int A_STAGES_FIT = SS ? 2 : static_cast<int>(TMEM_COLS - ACC_COLS) / A_STAGE_COLS;
   static constexpr int A_STAGES = A_STAGES_FIT > 4 ? 4 : A_STAGES_FIT;
   static constexpr int CHUNKS = W_ROW_BYTES / 16;
   static constexpr size_t SMEM_BYTES =
@@ -277,6 +280,18 @@ __device__ __forceinline__ void tc_mma(uint32_t d, uint32_t a, uint64_t bdesc, u
       "setp.ne.b32 q, %5, 0;\n\t"
       "@q tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
       "r"(a), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(issue)
+      : "memory");
+}
+
+// A from shared memory (descriptor), for bf16 weights staged by TMA
+__device__ __forceinline__ void tc_mma_ss(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate, uint32_t issue) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.ne.b32 q, %5, 0;\n\t"
+      "@q tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(issue)
       : "memory");
 }
 
@@ -514,6 +529,9 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = args.E;
   pdl_wait();
+  // the previous kernel's generic stores (the token rows this launch reads) must be
+  // visible to this launch's TMA (async proxy) reads
+  asm volatile("fence.proxy.async.global;" ::: "memory");
   // phase of an item: 0 = GEMM1 (or the single GEMM), 1 = GEMM2 of a fused launch
   auto is_g1 = [&](int ph) -> bool { return args.fused ? ph == 0 : GEMM1; };
 
@@ -553,7 +571,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
   if (threadIdx.x == 32) {
     for (int i = 0; i < WS; ++i) {
       mbar_init(&wfull[i], 1);
-      mbar_init(&wfree[i], DQ_WARPS);
+      mbar_init(&wfree[i], C::SS ? MMA_WARPS : DQ_WARPS);
     }
     for (int i = 0; i < BS; ++i) {
       mbar_init(&bfull[i], 1);
@@ -562,7 +580,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     for (int i = 0; i < 2 * AS; ++i) mbar_init(&a_full[i], 4);  // the tile's warpgroup of the step's group
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sc_full[i], 1);
-      mbar_init(&sc_empty[i], FAST ? DQ_WARPS + C::EPI_WARPS : DQ_WARPS);
+      mbar_init(&sc_empty[i], C::SS ? 1 : (FAST ? DQ_WARPS + C::EPI_WARPS : DQ_WARPS));
       mbar_init(&acc_full[i], MMA_WARPS);
       mbar_init(&acc_empty[i], C::EPI_WARPS);
     }
@@ -634,12 +652,14 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         const TcPhase& P = args.ph[item.ph];
         const int G = P.groups;
         const int sbuf = ii & 1;
-        if (!mbar_wait(&sc_empty[sbuf], ((ii >> 1) & 1) ^ 1, abort_flag, 0x100)) break;
-        const uint32_t sbytes = static_cast<uint32_t>(ROWS * G * 4);
-        mbar_expect_tx(&sc_full[sbuf], 2 * sbytes);
-        float* sdst = ssc + sbuf * (2 * ROWS * MAX_G);
-        bulk_load(sdst, P.scale + wrow_of(item, 0) * G, sbytes, &sc_full[sbuf]);
-        bulk_load(sdst + ROWS * MAX_G, P.scale + wrow_of(item, 1) * G, sbytes, &sc_full[sbuf]);
+        if (!C::SS) {
+          if (!mbar_wait(&sc_empty[sbuf], ((ii >> 1) & 1) ^ 1, abort_flag, 0x100)) break;
+          const uint32_t sbytes = static_cast<uint32_t>(ROWS * G * 4);
+          mbar_expect_tx(&sc_full[sbuf], 2 * sbytes);
+          float* sdst = ssc + sbuf * (2 * ROWS * MAX_G);
+          bulk_load(sdst, P.scale + wrow_of(item, 0) * G, sbytes, &sc_full[sbuf]);
+          bulk_load(sdst + ROWS * MAX_G, P.scale + wrow_of(item, 1) * G, sbytes, &sc_full[sbuf]);
+        }
         XP(0);
         const CUtensorMap* tw = item.ph == 0 ? &tm_w0 : &tm_w1;
         const int w0 = static_cast<int>(wrow_of(item, 0)), w1 = static_cast<int>(wrow_of(item, 1));
@@ -651,8 +671,16 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           XP(1);
           mbar_expect_tx(&wfull[rs], C::W_STAGE_BYTES);
           uint8_t* wdst = sw + rs * C::W_STAGE_BYTES;
-          tma_load_2d(wdst, tw, kc * C::W_ROW_BYTES, w0, &wfull[rs]);
-          tma_load_2d(wdst + C::W_TILE_BYTES, tw, kc * C::W_ROW_BYTES, w1, &wfull[rs]);
+          if (C::SS) {  // bf16 rows: two 64-element, 128-byte-swizzled boxes per tile
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              tma_load_2d(wdst + t * C::W_TILE_BYTES, tw, kc * KC, t ? w1 : w0, &wfull[rs]);
+              tma_load_2d(wdst + t * C::W_TILE_BYTES + ROWS * 128, tw, kc * KC + 64, t ? w1 : w0, &wfull[rs]);
+            }
+          } else {
+            tma_load_2d(wdst, tw, kc * C::W_ROW_BYTES, w0, &wfull[rs]);
+            tma_load_2d(wdst + C::W_TILE_BYTES, tw, kc * C::W_ROW_BYTES, w1, &wfull[rs]);
+          }
           XP(2);
           ++issued;
           if (++rs == WS) {
@@ -737,8 +765,8 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     XP_INIT
     {
       const uint32_t a_base = tmem + C::ACC_COLS;
-      int it = 0, rs = 0, ra = 0;
-      uint32_t rph = 0, raph = 0;  // token ring slot / phase and TMEM A stage / phase of step it
+      int it = 0, rs = 0, ra = 0, ws = 0;
+      uint32_t rph = 0, raph = 0, wph = 0;  // token ring, TMEM A stage, (SS) weight ring: slots and phases
       bool ok = true;
       for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
         const Item item = item_at(u);
@@ -769,7 +797,12 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           XP(4);
           if (!mbar_wait(&bfull[s], rph, abort_flag, 0x220 + s)) { ok = false; break; }
           XP(1);
-          if (!mbar_wait(&a_full[tile * AS + sa], raph, abort_flag, 0x230 + sa)) { ok = false; break; }
+          if (C::SS) {
+            if (!mbar_wait(&wfull[ws], wph, abort_flag, 0x240 + ws)) { ok = false; break; }
+          } else if (!mbar_wait(&a_full[tile * AS + sa], raph, abort_flag, 0x230 + sa)) {
+            ok = false;
+            break;
+          }
           XP(2);
           tc_fence_after();
           // descriptors advance by plain adds on the 16-byte-unit start address
@@ -783,9 +816,23 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
             const int j = jj * SPLIT + par;
             const uint64_t bdesc = bdesc0 + (j >> 2) * half_step + (j & 3) * 2;
             const uint32_t acc = jj > 0 ? 1u : first;
-            if (!LLQ_X_NOMMA) tc_mma(d, a_stage + j * 8, bdesc, idesc, acc, leader);
+            if (C::SS) {
+              // A = this tile's bf16 weights in shared memory, laid out like the token tile
+              const uint64_t adesc = make_sdesc(smem_u32(sw + ws * C::W_STAGE_BYTES + tile * C::W_TILE_BYTES)) +
+                                     (j >> 2) * static_cast<uint64_t>((ROWS * 128) >> 4) + (j & 3) * 2;
+              tc_mma_ss(d, adesc, bdesc, idesc, acc, leader);
+            } else if (!LLQ_X_NOMMA) {
+              tc_mma(d, a_stage + j * 8, bdesc, idesc, acc, leader);
+            }
           }
           tc_commit(&mdone[s], leader);
+          if (C::SS) {  // the step's MMAs also release the weight stage
+            tc_commit(&wfree[ws], leader);
+            if (++ws == WS) {
+              ws = 0;
+              wph ^= 1;
+            }
+          }
           if (!FAST && kc == kend - 1) tc_commit(&acc_full[C::ACC_BUFS == 2 ? (ii & 1) : 0], leader);
           XP(3);
           if (++rs == BS) {
@@ -852,6 +899,8 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           const int pc = c ^ (r & 7);  // 128-byte swizzle
           v[ci] = *reinterpret_cast<const uint4*>(wt + pc * 16);
         }
+        // our generic reads of the stage before the TMA (async proxy) refills it
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (stage_done && lane == 0) mbar_arrive(&wfree[s]);
         XP(2);
@@ -894,6 +943,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         }
         if (++ra == AS) ra = 0;
       }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // scale reads before the bulk refill
       __syncwarp();
       if (ok && lane == 0) mbar_arrive(&sc_empty[sbuf]);
     }
@@ -1005,6 +1055,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           if (lane == 0) mbar_arrive(&acc_empty[pb]);
         }
         if (!ok) break;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // scale reads before the bulk refill
         __syncwarp();
         if (lane == 0) mbar_arrive(&sc_empty[sbuf]);
 #pragma unroll
@@ -1120,8 +1171,10 @@ template <int BITS, int NTM>
 int phase_maps(const void* act, int64_t n_rows, int K, int E, int rows_total, const int8_t* q, CUtensorMap* tw,
                CUtensorMap* tb) {
   const uint64_t k_bytes = static_cast<uint64_t>(K) * BITS / 8;
-  int rc = make_map(tw, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, k_bytes, static_cast<uint64_t>(E) * rows_total, k_bytes,
-                    128, ROWS, CU_TENSOR_MAP_SWIZZLE_128B);
+  int rc = BITS == 16 ? make_map(tw, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, static_cast<uint64_t>(E) * rows_total,
+                                 k_bytes, 64, ROWS, CU_TENSOR_MAP_SWIZZLE_128B)
+                      : make_map(tw, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, k_bytes, static_cast<uint64_t>(E) * rows_total,
+                                 k_bytes, 128, ROWS, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   for (int i = 0; i < 4; ++i) {
     const uint32_t box = 16u << (i < 3 || NTM >= 128 ? i : 2);
@@ -1321,6 +1374,21 @@ int gemm2_tc(const void* h_sorted, const int32_t* offsets, const int32_t* sorted
 
 // token tiles are >= 64 rows, plus one partial tile per expert; one more slot counts CTAs
 int gemm12_counter_slots(int64_t n_rows, int E) { return static_cast<int>(n_rows / 16 + E + 2); }
+
+// GEMM1 + GEMM2 over bf16 weights dequantized beforehand (prefill-sized batches, where
+// each weight meets many token tiles): TMA brings both operands to shared memory and
+// the kernel's warps only load, multiply and run the epilogues
+int gemm12_fused_bf16_tc(const void* x_sorted, const int32_t* offsets, const int32_t* sorted_slots,
+                         const float* topk_w, int64_t n_rows, int E, int H, int I, const void* w1, const void* w2,
+                         void* h_sorted, void* y_slots, int* tile_done, cudaStream_t st) {
+  if (E < 1 || E > MAX_E || H % KC != 0 || I % KC != 0 || H > KC * MAX_G || I > KC * MAX_G || H % (2 * ROWS) != 0)
+    return fail(LLQ_EUNSUPPORTED, "tcgen05 bf16 expert GEMMs: unsupported shape");
+  const int tile_done_n = gemm12_counter_slots(n_rows, E) - 1;
+  return launch_fused<16, 128>(x_sorted, h_sorted, n_rows, offsets, E, H, I, static_cast<const int8_t*>(w1), nullptr,
+                               static_cast<const int8_t*>(w2), nullptr, 0, sorted_slots, topk_w, y_slots, tile_done,
+                               tile_done_n, st, nullptr);
+}
+
 
 int gemm12_fused_tc(const void* x_sorted, const int32_t* offsets, const int32_t* sorted_slots, const float* topk_w,
                     int64_t n_rows, int E, int H, int I, const int8_t* qw1, const float* sw1, const int8_t* qw2,

@@ -256,3 +256,25 @@ def test_fused_gemm12_equals_the_two_launches(T, bits):
         torch.cuda.synchronize()
         assert torch.equal(y, y_ref)
         assert int(counters.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_prefill_layer_on_dequantized_weights(bits):
+    """Prefill-sized calls (>= 512 routed rows per expert) dequantize the layer's weights once
+    (bit-identical to dequantize_tensor) and run both expert GEMMs with the bf16 weights
+    staged in shared memory by TMA.  Same oracle and tolerance as the packed path, and the
+    packed two-launch path as a second reference."""
+    from llada_quant_b200 import _lib, ops
+    T, E, H, I, k = 4096, 16, 1024, 512, 2
+    r1, r2 = _quantize(E, H, I, bits, seed=11)
+    x = synthetic_tokens(T, H, seed=12).cuda()
+    tw, ids = random_routing(T, E, k, seed=13, skew=0.5)
+    tw_d, ids_d = torch.from_numpy(tw).cuda(), torch.from_numpy(ids).cuda()
+    out = ops.fused_moe_packed(x, r1.q, r1.scale, r2.q, r2.scale, tw_d, ids_d, bits, _lib.LLQ_GEMM_AUTO)
+    ref = M.fused_moe_packed(to_np(x), to_np(r1.q), to_np(r1.scale), to_np(r2.q), to_np(r2.scale), tw, ids, bits)
+    _assert_layer_close(to_np(out), ref)
+    off, slots = ops.moe_align(ids_d, E)
+    h = ops.moe_gemm1(ops.moe_permute(x, slots, k), off, r1.q, r1.scale, bits, _lib.LLQ_GEMM_TCGEN05)
+    y = ops.moe_gemm2(h, off, slots, tw_d, r2.q, r2.scale, bits, _lib.LLQ_GEMM_TCGEN05)
+    packed = ops.moe_combine(y, k)
+    _assert_layer_close(to_np(out), to_np(packed))
