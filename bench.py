@@ -879,9 +879,45 @@ def run_c4(args):
     print(json.dumps(line), flush=True)
 
 
+def kernel_case_pack():
+    """The pack kernel on the C3 w1 tensor: one bf16 [64, 2048, 2048] weight (537 MB)
+    quantized to packed INT4 + fp32 scales (amax, group 128), twice."""
+    import torch
+    from llada_quant_b200 import symmetric as G
+    device = torch.device("cuda", 0)
+    w = (torch.randn(E, 2 * I, H, generator=torch.Generator(device=device).manual_seed(0), device=device)
+         * 0.02).to(torch.bfloat16)
+    for _ in range(2):
+        r = G.quantize_tensor(w, bits=BITS, group_size=GROUP)
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel_case": "pack", "bytes_in": w.numel() * 2,
+                      "bytes_out": r.q.numel() + r.scale.numel() * 4}))
+
+
+def kernel_case_c4():
+    """One C4-sized layer call (T = 32768 tokens, top-8): the weights dequantized once, then the
+    bf16 expert GEMMs from shared memory; twice."""
+    import torch
+    from llada_quant_b200 import ops
+    device = torch.device("cuda", 0)
+    layers, gate_w = make_layers(device, 1, E, 0)
+    lay = layers[0]
+    x = torch.randn(C4_TOKENS, H, generator=torch.Generator(device=device).manual_seed(2),
+                    device=device).to(torch.bfloat16)
+    for _ in range(2):
+        tw, ids, _ = ops._route_impl(x, gate_w, TOPK, None, False)
+        y = ops._fused_moe_packed_impl(x, lay.qw1, lay.sw1, lay.qw2, lay.sw2, tw, ids, BITS, 0)
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel_case": "C4 layer", "out_abs_mean": float(y.float().abs().mean())}))
+
+
 def kernel_case(args):
     """One C3 layer weight set, route -> align -> permute -> fused GEMM1+GEMM2 (exact; two
     launches in fast mode) -> combine, twice."""
+    if args.case == "pack":
+        return kernel_case_pack()
+    if args.case == "c4":
+        return kernel_case_c4()
     import torch
     from llada_quant_b200 import ops
     from llada_quant_b200.fused_moe import IMPL
@@ -925,6 +961,9 @@ def main():
     ap.add_argument("--workload", choices=["c3", "c4"], default="c3",
                     help="c3: one LLaDA-MoE layer at 256 tokens (default, HBM-bound); c4: the 16-layer "
                          "stack over batch 32 x seq 1024 tokens (tensor-bound)")
+    ap.add_argument("--case", choices=["c3", "pack", "c4"], default="c3",
+                    help="with --kernel-case: which kernels to run (the C3 layer, the pack kernel on C3 w1, "
+                         "one C4-sized layer)")
     ap.add_argument("--kernel-case", action="store_true",
                     help="run the C3 layer's kernels twice on one small input set and exit "
                          "(the command the ncu captures under profiles/ were taken on)")

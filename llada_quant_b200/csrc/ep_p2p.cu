@@ -119,6 +119,8 @@ struct EpWorkspace {
   void* h_sorted;
   int32_t* counters;  // the fused GEMMs' tile counters
   int n_counters;
+  void* w1_bf16;      // windows that can hold prefill-sized calls: the shard's weights in bf16
+  void* w2_bf16;
   size_t total;
 };
 
@@ -139,6 +141,11 @@ EpWorkspace carve_ep(void* base, int R, int cap, int E, int H, int I) {
   w.h_sorted = take(static_cast<size_t>(n) * I * 2 + 4096);
   w.n_counters = gemm12_counter_slots(n, E);
   w.counters = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * w.n_counters));
+  w.w1_bf16 = w.w2_bf16 = nullptr;
+  if (n >= static_cast<int64_t>(E) * kPrefillRowsPerExpert) {
+    w.w1_bf16 = take(static_cast<size_t>(E) * 2 * I * H * 2);
+    w.w2_bf16 = take(static_cast<size_t>(E) * H * I * 2);
+  }
   w.total = off;
   return w;
 }
@@ -284,6 +291,17 @@ int llq_ep_experts(void* window, void* const* peers, int rank, int world, int ca
   sc.me = rank;
   sc.epoch = epoch;
   sc.done = ep_done(mine, L, 1);
+  if (!fast && ws.w1_bf16 != nullptr && rows_hint >= static_cast<int64_t>(E) * kPrefillRowsPerExpert) {
+    // prefill-sized call: the shard's weights dequantized once, bf16 GEMMs from shared memory
+    rc = dequantize_impl(qw1, sw1, static_cast<int64_t>(E) * 2 * I, H, bits, group_size, bits == 4, ws.w1_bf16,
+                         LLQ_BF16, st);
+    if (rc) return rc;
+    rc = dequantize_impl(qw2, sw2, static_cast<int64_t>(E) * H, I, bits, group_size, bits == 4, ws.w2_bf16,
+                         LLQ_BF16, st);
+    if (rc) return rc;
+    return gemm12_fused_bf16_tc(ws.x_sorted, ws.offsets, ws.sorted_slots, reinterpret_cast<const float*>(mine + L.wts),
+                                n, E, H, I, ws.w1_bf16, ws.w2_bf16, ws.h_sorted, nullptr, ws.counters, st, &sc);
+  }
   if (!fast)  // GEMM1 and GEMM2 in one launch; GEMM2 rows go straight to the source ranks
     return gemm12_fused_tc(ws.x_sorted, ws.offsets, ws.sorted_slots, reinterpret_cast<const float*>(mine + L.wts), n,
                            E, H, I, qw1, sw1, qw2, sw2, bits, group_size, ws.h_sorted, nullptr, ws.counters, st,

@@ -44,7 +44,8 @@ int gemm12_fused_tc(const void* x_sorted, const int32_t* offsets, const int32_t*
                     cudaStream_t st, int64_t rows_hint = -1, const EpScatter* ep = nullptr);
 int gemm12_fused_bf16_tc(const void* x_sorted, const int32_t* offsets, const int32_t* sorted_slots,
                          const float* topk_w, int64_t n_rows, int E, int H, int I, const void* w1, const void* w2,
-                         void* h_sorted, void* y_slots, int* tile_done, cudaStream_t st);
+                         void* h_sorted, void* y_slots, int* tile_done, cudaStream_t st,
+                         const EpScatter* ep = nullptr);
 // routed rows per expert from which a layer dequantizes its weights once and runs bf16 GEMMs
 constexpr int64_t kPrefillRowsPerExpert = 512;
 int dense_linear_tc(const void* x, int64_t M, int K, int N, const int8_t* q, const float* scale, int bits,

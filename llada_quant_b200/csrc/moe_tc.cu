@@ -86,20 +86,23 @@ struct Cfg {
   // BITS == 16: the weights are already bf16 (dequantized once per layer call for
   // prefill-sized batches) and reach the tensor cores from shared memory by TMA
   static constexpr bool SS = BITS == 16;
-  static constexpr int W_ROW_BYTES = KC * BITS / 8;  // packed bytes of one row per K step
+  // K per step: 128 (one scale group) for packed weights; 64 for bf16 weights, whose
+  // stages are then small enough for 4-deep rings of both operands
+  static constexpr int KS = SS ? 64 : KC;
+  static constexpr int W_ROW_BYTES = KS * BITS / 8;  // packed bytes of one row per K step
   // a weight load brings 128 bytes of each row (two K steps at INT4): twice the
   // DRAM burst of one step, half the TMA row requests per weight byte
   static constexpr int W_STEPS = SS ? 1 : 128 / W_ROW_BYTES;
   static constexpr int W_LOAD_BYTES = W_ROW_BYTES * W_STEPS;
   static constexpr int W_TILE_BYTES = ROWS * W_LOAD_BYTES;
   static constexpr int W_STAGE_BYTES = 2 * W_TILE_BYTES;
-  static constexpr int B_STAGE_BYTES = NTM * KC * 2;
+  static constexpr int B_STAGE_BYTES = NTM * KS * 2;
   static constexpr int SCALE_BUF_BYTES = SS ? 0 : 2 * ROWS * MAX_G * 4;
   // Two rings: packed weights, released as soon as the dequantizing warps have
   // copied them to registers, and token tiles, released when the step's MMAs
   // complete.  Weight slots thus turn over at the speed of HBM, independently
   // of the MMA pipeline, and the weight ring takes what shared memory is left.
-  static constexpr int B_STAGES = SS ? 2 : 3;
+  static constexpr int B_STAGES = SS ? 4 : 3;
   static constexpr int W_STAGES_FIT =
       (220 * 1024 - 2 * SCALE_BUF_BYTES - B_STAGES * B_STAGE_BYTES) / W_STAGE_BYTES;
   static constexpr int W_STAGES = W_STAGES_FIT > 8 ? 8 : W_STAGES_FIT;
@@ -634,7 +637,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
   };
   // K steps of an item: [kbeg, kbeg + kper)
   auto k_range = [&](const Item& it, int& kbeg, int& kper) {
-    const int kch = args.ph[it.ph].K / KC;
+    const int kch = args.ph[it.ph].K / C::KS;
     kper = kch / (it.ph ? 1 : args.ksplit);
     kbeg = it.ks * kper;
   };
@@ -674,8 +677,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           if (C::SS) {  // bf16 rows: two 64-element, 128-byte-swizzled boxes per tile
 #pragma unroll
             for (int t = 0; t < 2; ++t) {
-              tma_load_2d(wdst + t * C::W_TILE_BYTES, tw, kc * KC, t ? w1 : w0, &wfull[rs]);
-              tma_load_2d(wdst + t * C::W_TILE_BYTES + ROWS * 128, tw, kc * KC + 64, t ? w1 : w0, &wfull[rs]);
+              tma_load_2d(wdst + t * C::W_TILE_BYTES, tw, kc * C::KS, t ? w1 : w0, &wfull[rs]);
             }
           } else {
             tma_load_2d(wdst, tw, kc * C::W_ROW_BYTES, w0, &wfull[rs]);
@@ -736,10 +738,10 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           XP(3);
           if (!mbar_wait(&mdone[rs], rph ^ 1, abort_flag, 0x118 + rs)) { ok = false; break; }
           XP(1);
-          mbar_expect_tx(&bfull[rs], 2 * box * 128);
+          mbar_expect_tx(&bfull[rs], (C::KS / 64) * box * 128);
           uint8_t* bdst = sb + rs * C::B_STAGE_BYTES;
-          tma_load_2d(bdst, tb, kc * KC, item.row0, &bfull[rs]);
-          tma_load_2d(bdst + box * 128, tb, kc * KC + 64, item.row0, &bfull[rs]);
+          tma_load_2d(bdst, tb, kc * C::KS, item.row0, &bfull[rs]);
+          if (C::KS == 128) tma_load_2d(bdst + box * 128, tb, kc * C::KS + 64, item.row0, &bfull[rs]);
           XP(2);
           ++issued;
           if (++rs == BS) {
@@ -812,7 +814,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           const uint32_t d = tile ? d1 : d0;
           const uint32_t first = FAST ? 0u : (kc > kbeg ? 1u : 0u);
 #pragma unroll
-          for (int jj = 0; jj < KC / 16 / SPLIT; ++jj) {
+          for (int jj = 0; jj < C::KS / 16 / SPLIT; ++jj) {
             const int j = jj * SPLIT + par;
             const uint64_t bdesc = bdesc0 + (j >> 2) * half_step + (j & 3) * 2;
             const uint32_t acc = jj > 0 ? 1u : first;
@@ -1380,13 +1382,13 @@ int gemm12_counter_slots(int64_t n_rows, int E) { return static_cast<int>(n_rows
 // the kernel's warps only load, multiply and run the epilogues
 int gemm12_fused_bf16_tc(const void* x_sorted, const int32_t* offsets, const int32_t* sorted_slots,
                          const float* topk_w, int64_t n_rows, int E, int H, int I, const void* w1, const void* w2,
-                         void* h_sorted, void* y_slots, int* tile_done, cudaStream_t st) {
+                         void* h_sorted, void* y_slots, int* tile_done, cudaStream_t st, const EpScatter* ep) {
   if (E < 1 || E > MAX_E || H % KC != 0 || I % KC != 0 || H > KC * MAX_G || I > KC * MAX_G || H % (2 * ROWS) != 0)
     return fail(LLQ_EUNSUPPORTED, "tcgen05 bf16 expert GEMMs: unsupported shape");
   const int tile_done_n = gemm12_counter_slots(n_rows, E) - 1;
   return launch_fused<16, 128>(x_sorted, h_sorted, n_rows, offsets, E, H, I, static_cast<const int8_t*>(w1), nullptr,
                                static_cast<const int8_t*>(w2), nullptr, 0, sorted_slots, topk_w, y_slots, tile_done,
-                               tile_done_n, st, nullptr);
+                               tile_done_n, st, ep);
 }
 
 
@@ -1415,10 +1417,14 @@ int gemm12_fused_tc(const void* x_sorted, const int32_t* offsets, const int32_t*
 
 namespace llq {
 
+// A dense layer takes 128-token tiles only above this many rows: up to it, 64-token tiles
+// keep the deeper weight ring, and the tiles sharing a weight block read it from L2
+constexpr int64_t kDenseWideRows = 128;
+
 // K slices for a dense layer: enough work items to cover the SMs, each slice a
 // whole number of 128-wide K steps
 int dense_ksplit(int64_t M, int K, int N) {
-  const int ntm = M > 96 ? 128 : 64;
+  const int ntm = M > kDenseWideRows ? 128 : 64;
   const int64_t items = (M + ntm - 1) / ntm * (N / (2 * ROWS));
   const int kch = K / KC;
   int ks = 1;
@@ -1436,7 +1442,7 @@ int dense_linear_tc(const void* x, int64_t M, int K, int N, const int8_t* q, con
   if (ks > 1 && (workspace == nullptr || ws_bytes < need))
     return fail(LLQ_ENOSPACE, "quant_linear workspace needs %zu bytes, got %zu", need, ws_bytes);
   float* partial = static_cast<float*>(workspace);
-  if (M > 96) {
+  if (M > kDenseWideRows) {
     return bits == 4 ? dense_tc<4, 128>(x, M, K, N, q, scale, group_size, out, ks, partial, st)
                      : dense_tc<8, 128>(x, M, K, N, q, scale, group_size, out, ks, partial, st);
   }

@@ -35,6 +35,25 @@ __device__ __forceinline__ float quant_code(float x, float safe, float qmin, flo
   return fminf(fmaxf(t, qmin), qmax);
 }
 
+// rint(x / safe) through the reciprocal: t = x * fl(1/safe) is within 3 ulps of the
+// IEEE quotient fl(x / safe), so both round to the same integer unless a half-integer
+// lies within that distance -- detected (|frac(t) - 1/2| < 2^-12, far wider than 3 ulps
+// at the |t| <= 128.5 of INT4/INT8 codes) and then answered by the IEEE division itself.
+__device__ __noinline__ float exact_code(float x, float safe) { return rintf(__fdiv_rn(x, safe)); }
+
+__device__ __forceinline__ float quant_code_recip(float x, float safe, float inv, float qmin, float qmax) {
+  const float t = __fmul_rn(x, inv);
+  float r = rintf(t);
+  // (also when t is huge, infinite or NaN: a subnormal scale whose reciprocal overflows)
+  const bool near = fabsf(fabsf(t - r) - 0.5f) < 0x1p-12f || !(fabsf(t) <= 0x1p20f);
+  if (__builtin_expect(near, 0)) r = exact_code(x, safe);
+  return fminf(fmaxf(r, qmin), qmax);
+}
+
+// low byte of a code in [-128, 127] held as a float, without a float-to-int conversion:
+// 1.5 * 2^23 + r keeps r, two's complement, in the low mantissa bits
+__device__ __forceinline__ uint32_t code_bits(float r) { return __float_as_uint(__fadd_rn(r, 12582912.0f)); }
+
 __device__ __forceinline__ float err_term(float x, float safe, float qmin, float qmax) {
   float t = quant_code(x, safe, qmin, qmax);
   float d = __fsub_rn(__fmul_rn(t, safe), x);
@@ -201,13 +220,22 @@ __global__ void __launch_bounds__(256) quantize_g128_bf16_kernel(const uint4* __
   const float qmin = -qmax - 1.f;
   // each warp iteration covers 2 * kG128Unroll groups; the loop is warp-uniform so that
   // the half-warp shuffles always see a converged warp
-  for (int64_t base = warp * 2 * kG128Unroll; base < ngroups; base += nwarps * 2 * kG128Unroll) {
-    uint4 v[kG128Unroll];
+  // software-pipelined: the next iteration's loads are in flight while this one computes
+  const int64_t step = nwarps * 2 * kG128Unroll;
+  uint4 nxt[kG128Unroll];
+  auto load = [&](int64_t base, uint4 (&v)[kG128Unroll]) {
 #pragma unroll
     for (int u = 0; u < kG128Unroll; ++u) {
       const int64_t g = base + 2 * u + (lane >> 4);
       v[u] = g < ngroups ? __ldcs(w + g * 16 + sub) : make_uint4(0, 0, 0, 0);
     }
+  };
+  load(warp * 2 * kG128Unroll, nxt);
+  for (int64_t base = warp * 2 * kG128Unroll; base < ngroups; base += step) {
+    uint4 v[kG128Unroll];
+#pragma unroll
+    for (int u = 0; u < kG128Unroll; ++u) v[u] = nxt[u];
+    load(base + step, nxt);
 #pragma unroll
     for (int u = 0; u < kG128Unroll; ++u) {
       const int64_t g = base + 2 * u + (lane >> 4);
@@ -225,22 +253,23 @@ __global__ void __launch_bounds__(256) quantize_g128_bf16_kernel(const uint4* __
       for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       const float sc = apply_scale_round(__fdiv_rn(amax, qmax), scale_round);
       const float safe = sc > 0.f ? sc : 1.f;
+      const float inv = __frcp_rn(safe);
       if (g >= ngroups) continue;
       if (sub == 0) scale_out[g] = sc;
-      int c[8];
+      uint32_t c[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) c[i] = static_cast<int>(quant_code(x[i], safe, qmin, qmax));
+      for (int i = 0; i < 8; ++i) c[i] = code_bits(quant_code_recip(x[i], safe, inv, qmin, qmax));
       if (PACK4) {
         uint32_t b = 0;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) b |= static_cast<uint32_t>(c[i] & 0xF) << (4 * i);
+        for (int i = 0; i < 8; ++i) b |= (c[i] & 0xFu) << (4 * i);
         reinterpret_cast<uint32_t*>(q)[g * 16 + sub] = b;
       } else {
         uint32_t lo = 0, hi = 0;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          lo |= static_cast<uint32_t>(c[i] & 0xFF) << (8 * i);
-          hi |= static_cast<uint32_t>(c[i + 4] & 0xFF) << (8 * i);
+          lo |= (c[i] & 0xFFu) << (8 * i);
+          hi |= (c[i + 4] & 0xFFu) << (8 * i);
         }
         reinterpret_cast<uint2*>(q)[g * 16 + sub] = make_uint2(lo, hi);
       }

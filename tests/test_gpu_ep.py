@@ -18,7 +18,7 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-E, H, I, K, T_RANK = 64, 2048, 1024, 8, 128
+E, H, I, K = 64, 2048, 1024, 8
 
 
 def _port():
@@ -29,7 +29,7 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, path, transport):
+def _worker(rank, world, port, path, transport, T_RANK):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -66,8 +66,9 @@ def _worker(rank, world, port, path, transport):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("transport", ["nccl", "window"])
-def test_ep_matches_single_gpu(tmp_path, transport):
+@pytest.mark.parametrize("transport,T_RANK", [("nccl", 128), ("window", 128), ("window", 2048)])
+def test_ep_matches_single_gpu(tmp_path, transport, T_RANK):
+    """T_RANK=2048 (16384 routed rows per rank): the prefill path, weights dequantized once per call."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
@@ -77,7 +78,7 @@ def test_ep_matches_single_gpu(tmp_path, transport):
     from oracle import moe as M
     world = 2
     path = str(tmp_path / "ep")
-    mp.start_processes(_worker, args=(world, _port(), path, transport), nprocs=world, join=True, start_method="spawn")
+    mp.start_processes(_worker, args=(world, _port(), path, transport, T_RANK), nprocs=world, join=True, start_method="spawn")
     got = np.concatenate([np.load(f"{path}.{r}.npy") for r in range(world)])
     g = torch.Generator().manual_seed(0)
     w1 = (torch.randn(E, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16)

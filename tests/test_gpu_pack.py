@@ -181,3 +181,29 @@ def test_zero_tensor_and_scale_dtype():
     q, s, *_ = S.quantize_tensor(w.cpu().numpy(), bits=4, group_size=64)
     # the bf16 scale is the fp32 amax scale rounded once
     assert np.array_equal(rb.scale.float().cpu().numpy(), S.round_to_bf16(s))
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_amax_codes_at_half_integer_quotients(bits):
+    """The bandwidth pack kernel divides through the reciprocal and falls back to IEEE
+    division near half-integers; codes whose exact quotient is n + 1/2 (ties to even) or a
+    few ulps either side must equal the reference's round(w / s)."""
+    from llada_quant_b200 import symmetric as G
+    qmax = 7 if bits == 4 else 127
+    rng = np.random.default_rng(5)
+    rows = []
+    for s_mult in (1.0, 3.0, 0.75, 0.015625, 1.0 / 3.0):
+        amax = qmax * s_mult
+        for _ in range(8):
+            n = rng.integers(-qmax, qmax, size=127)
+            base = (n + 0.5) * s_mult
+            # exact half-integer quotients, and their bf16 neighbours one or two ulps away
+            jitter = torch.from_numpy(rng.choice([-2, -1, 0, 0, 0, 1, 2], size=127).astype(np.int16))
+            row = torch.from_numpy(base.astype(np.float32)).to(torch.bfloat16)
+            row = (row.view(torch.int16) + jitter * (row != 0)).view(torch.bfloat16)
+            rows.append(torch.cat([torch.tensor([amax]).to(torch.bfloat16), row]))
+    w = torch.stack(rows)
+    r = G.quantize_tensor(w.cuda(), bits=bits, group_size=128)
+    q_ref, s_ref, *_ = S.quantize_tensor(w.float().numpy(), bits=bits, group_size=128)
+    assert np.array_equal(to_np(r.scale).reshape(-1), np.asarray(s_ref).reshape(-1))
+    assert np.array_equal(to_np(r.q), np.asarray(q_ref))
