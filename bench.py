@@ -736,6 +736,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     extras = {}
     if world == 1 and not args.no_c4:
         extras["c4"] = measure_c4(args, steps=3, warmup=1)
+        extras["pack"] = measure_pack(device)
     if world > 1:
         from llada_quant_b200 import ep as _ep
         extras["phases"] = {
@@ -808,6 +809,37 @@ def c4_flops() -> float:
     """Algorithmic FLOPs of one C4 step: 16 layers x (router + GEMM1 + GEMM2) over 32768 tokens."""
     per_layer = 2.0 * C4_TOKENS * TOPK * (2 * I * H + H * I) + 2.0 * C4_TOKENS * H * E
     return per_layer * C4_LAYERS
+
+
+def measure_pack(device) -> dict:
+    """The quantize-and-pack kernel on the C3 w1 tensor (bf16 [64, 2048, 2048], amax, INT4
+    group 128): HBM bytes it must move (bf16 read, packed codes + fp32 scales written) over its
+    CUDA-event time, two rotated copies so that no call reads its input from L2."""
+    import torch
+    from llada_quant_b200 import ops
+    g = torch.Generator(device=device).manual_seed(0)
+    ws = [(torch.randn(E, 2 * I, H, generator=g, device=device) * 0.02).to(torch.bfloat16) for _ in range(2)]
+    q = torch.empty(E, 2 * I, H // 2, dtype=torch.int8, device=device)
+    sc = torch.empty(E, 2 * I, H // GROUP, dtype=torch.float32, device=device)
+    from llada_quant_b200._lib import check, load, LLQ_BF16, LLQ_F32, LLQ_SEARCH_AMAX
+    lib = load()
+    st = torch.cuda.current_stream(device).cuda_stream
+
+    def call(i):
+        w = ws[i & 1]
+        check(lib.llq_quantize_pack(w.data_ptr(), LLQ_BF16, E * 2 * I, H, BITS, GROUP, LLQ_SEARCH_AMAX, 24, 0.5,
+                                    LLQ_F32, 1, q.data_ptr(), sc.data_ptr(), st), "quantize_pack")
+    for i in range(3):
+        call(i)
+    ms, repeats, timed_s = timed_steps(call, 10, 1, device, lambda: None, min_seconds=0.5)
+    algo = ws[0].numel() * 2 + q.numel() + sc.numel() * 4
+    hbm, kind = read_peaks()
+    gbs = algo / (ms / 1e3) / 1e9
+    del ws
+    torch.cuda.empty_cache()
+    return {"kernel": "quantize_g128_bf16_kernel (amax, INT4 g128) on C3 w1", "algorithmic_bytes": algo,
+            "launch_ms": round(ms, 5), "achieved": round(gbs, 1), "unit": "GB/s", "peak": hbm,
+            "frac": round(gbs / hbm, 4), "peak_source": kind, "timed_region_s": round(timed_s, 3)}
 
 
 def read_tensor_peak():

@@ -258,10 +258,8 @@ int llq_fused_moe_packed(const void* x, const int8_t* qw1, const float* sw1, con
                                     "I %% 128 == 0, H %% 256 == 0, group %% 128 == 0)");
     rc = permute_impl(x, T, H, k, ws.sorted_slots, ws.x_sorted, st, 1);
     if (rc) return rc;
-    rc = gemm1_tc(ws.x_sorted, ws.offsets, n, E, H, I, qw1, sw1, bits, group_size, ws.h_sorted, true, st);
-    if (rc) return rc;
-    rc = gemm2_tc(ws.h_sorted, ws.offsets, ws.sorted_slots, topk_w, n, E, H, I, qw2, sw2, bits, group_size,
-                  ws.y_slots, true, st);
+    rc = gemm12_fused_tc(ws.x_sorted, ws.offsets, ws.sorted_slots, topk_w, n, E, H, I, qw1, sw1, qw2, sw2, bits,
+                         group_size, ws.h_sorted, ws.y_slots, ws.tile_done, st, -1, nullptr, true);
     if (rc) return rc;
     return combine_impl(ws.y_slots, T, k, H, out, st);
   }

@@ -41,7 +41,8 @@ int gemm12_counter_slots(int64_t n_rows, int E);
 int gemm12_fused_tc(const void* x_sorted, const int32_t* offsets, const int32_t* sorted_slots, const float* topk_w,
                     int64_t n_rows, int E, int H, int I, const int8_t* qw1, const float* sw1, const int8_t* qw2,
                     const float* sw2, int bits, int group_size, void* h_sorted, void* y_slots, int* tile_done,
-                    cudaStream_t st, int64_t rows_hint = -1, const EpScatter* ep = nullptr);
+                    cudaStream_t st, int64_t rows_hint = -1, const EpScatter* ep = nullptr,
+                    bool fast = false);
 int gemm12_fused_bf16_tc(const void* x_sorted, const int32_t* offsets, const int32_t* sorted_slots,
                          const float* topk_w, int64_t n_rows, int E, int H, int I, const void* w1, const void* w2,
                          void* h_sorted, void* y_slots, int* tile_done, cudaStream_t st,

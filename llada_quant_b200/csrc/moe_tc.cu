@@ -48,6 +48,9 @@
 #ifndef LLQ_X_NODQ
 #define LLQ_X_NODQ 0
 #endif
+#ifndef LLQ_X_EPWF
+#define LLQ_X_EPWF 16
+#endif
 #ifndef LLQ_X_PROF
 #define LLQ_X_PROF 0
 #endif
@@ -122,7 +125,7 @@ struct Cfg {
   // that take alternate K steps, so that one group's waits overlap the other's math
   static constexpr int DQ_GROUPS = FAST ? 1 : LLQ_X_DQG;
   static constexpr int DQ_WARPS = SS ? 0 : 8 * DQ_GROUPS;
-  static constexpr int EPI_WARPS = LLQ_X_EPW;  // token groups of one warpgroup each
+  static constexpr int EPI_WARPS = FAST ? LLQ_X_EPWF : LLQ_X_EPW;  // token groups of one warpgroup each
   static constexpr int FIRST_MMA = 2;  // warp 0 loads weights and scales, warp 1 token tiles
   static constexpr int FIRST_DQ = FIRST_MMA + MMA_WARPS;
   static constexpr int FIRST_EPI = FIRST_DQ + DQ_WARPS;
@@ -792,7 +795,9 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           uint32_t d0 = acc_base + par * NTM, d1 = acc_base + (SPLIT + par) * NTM;
           if (FAST) {
             const int pb = it & 1;
+            XP(4);
             if (!mbar_wait(&acc_empty[pb], ((it >> 1) & 1) ^ 1, abort_flag, 0x210 + pb)) { ok = false; break; }
+            XP(0);
             d0 = tmem + pb * 2 * NTM;
             d1 = d0 + NTM;
           }
@@ -1032,8 +1037,10 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         const float* s1row = s0row + ROWS * MAX_G;
         for (int kc = 0; kc < P.K / KC; ++kc, ++it) {
           const int pb = it & 1;
+          XP(2);
           if (!mbar_wait(&mdone[it % BS], (it / BS) & 1, abort_flag, 0x410 + pb)) { ok = false; break; }
           tc_fence_after();
+          XP(0);
           const int gi = P.group > 0 ? (kc * KC) / P.group : 0;
           const float s0 = s0row[gi], s1 = s1row[gi];
           const uint32_t p0 = tmem + lane_addr + pb * 2 * NTM + t_begin, p1 = p0 + NTM;
@@ -1055,6 +1062,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[pb]);
+          XP(1);
         }
         if (!ok) break;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // scale reads before the bulk refill
@@ -1098,12 +1106,12 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[ab]);
         XP(1);
-        if (args.fused && item.ph == 0) {
-          // this warp's rows of h are stored: count it for the token tile's GEMM2 items
-          __threadfence();
-          __syncwarp();
-          if (lane == 0) atomicAdd(args.tile_done + item.tg, 1);
-        }
+      }
+      if (args.fused && item.ph == 0) {
+        // this warp's rows of h are stored: count it for the token tile's GEMM2 items
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(args.tile_done + item.tg, 1);
       }
     }
     if (warp == FIRST_EPI) XP_SAVE(4);
@@ -1245,7 +1253,7 @@ int launch_tc(const void* act, int64_t n_rows, const int32_t* offsets, int E, in
 
 // GEMM1 and GEMM2 of one layer in one persistent launch (exact mode): GEMM2 items
 // follow the GEMM1 items and start as soon as their token tile's h rows are stored
-template <int BITS, int NTM>
+template <int BITS, int NTM, bool FAST = false>
 int launch_fused(const void* x_sorted, void* h_sorted, int64_t n_rows, const int32_t* offsets, int E, int H, int I,
                  const int8_t* qw1, const float* sw1, const int8_t* qw2, const float* sw2, int group_size,
                  const int32_t* sorted_slots, const float* topk_w, void* y_slots, int* tile_done,
@@ -1271,7 +1279,7 @@ int launch_fused(const void* x_sorted, void* h_sorted, int64_t n_rows, const int
   a.tile_done_n = tile_done_n;
   a.ep_on = ep != nullptr;  // GEMM2 rows go to the source ranks' windows
   if (ep != nullptr) a.ep = *ep;
-  return launch_kernel<true, BITS, false, NTM>(tw, tb, a, st);
+  return launch_kernel<true, BITS, FAST, NTM>(tw, tb, a, st);
 }
 
 // decode tiles (64 tokens) unless the average expert holds more than 96 rows
@@ -1395,10 +1403,15 @@ int gemm12_fused_bf16_tc(const void* x_sorted, const int32_t* offsets, const int
 int gemm12_fused_tc(const void* x_sorted, const int32_t* offsets, const int32_t* sorted_slots, const float* topk_w,
                     int64_t n_rows, int E, int H, int I, const int8_t* qw1, const float* sw1, const int8_t* qw2,
                     const float* sw2, int bits, int group_size, void* h_sorted, void* y_slots, int* tile_done,
-                    cudaStream_t st, int64_t rows_hint, const EpScatter* ep) {
+                    cudaStream_t st, int64_t rows_hint, const EpScatter* ep, bool fast) {
   if (!tc_supported(E, I, H, bits, group_size, true) || !tc_supported(E, H, I, bits, group_size, false))
     return fail(LLQ_EUNSUPPORTED, "tcgen05 expert GEMMs: unsupported shape");
   const int tile_done_n = gemm12_counter_slots(n_rows, E) - 1;
+  if (fast) {  // scale-after-MMA mode: INT4, 64-token tiles (token rows K-interleaved by the permute)
+    if (bits != 4) return fail(LLQ_EUNSUPPORTED, "fast dequantization is INT4 only");
+    return launch_fused<4, 64, true>(x_sorted, h_sorted, n_rows, offsets, E, H, I, qw1, sw1, qw2, sw2, group_size,
+                                     sorted_slots, topk_w, y_slots, tile_done, tile_done_n, st, ep);
+  }
   if (rows_hint < 0) rows_hint = n_rows;
   const bool wide = rows_hint > static_cast<int64_t>(E) * 96;
   if (bits == 4)
