@@ -39,40 +39,6 @@
 #include "llq_common.cuh"
 #include "ep_window.cuh"
 
-#ifndef LLQ_X_NOMMA
-#define LLQ_X_NOMMA 0
-#endif
-#ifndef LLQ_X_NOTOK
-#define LLQ_X_NOTOK 0
-#endif
-#ifndef LLQ_X_NODQ
-#define LLQ_X_NODQ 0
-#endif
-#ifndef LLQ_X_EPWF
-#define LLQ_X_EPWF 16
-#endif
-#ifndef LLQ_X_PROF
-#define LLQ_X_PROF 0
-#endif
-#if LLQ_X_PROF
-__device__ long long g_xprof[256][48];
-#define XP_INIT long long xp_acc[8] = {0, 0, 0, 0, 0, 0, 0, 0}; long long xp_last = clock64();
-#define XP(i) do { const long long xp_n = clock64(); xp_acc[i] += xp_n - xp_last; xp_last = xp_n; } while (0)
-#define XP_SAVE(role) do { if (lane == 0) for (int xi = 0; xi < 8; ++xi) g_xprof[blockIdx.x][(role) * 8 + xi] = xp_acc[xi]; } while (0)
-#else
-#define XP_INIT
-#define XP(i) do {} while (0)
-#define XP_SAVE(role) do {} while (0)
-#endif
-#ifndef LLQ_X_SPLIT
-#define LLQ_X_SPLIT 1
-#endif
-#ifndef LLQ_X_DQG
-#define LLQ_X_DQG 1
-#endif
-#ifndef LLQ_X_EPW
-#define LLQ_X_EPW 8
-#endif
 namespace llq {
 
 namespace {
@@ -117,15 +83,15 @@ struct Cfg {
   // (measured on B200 at C3: splitting K across four issuers with 16 dequant
   // warps gained nothing over two issuers with 8 -- exact dequantization is
   // then ALU-bound -- so SPLIT stays 1; the code keeps both layouts correct)
-  static constexpr int SPLIT = LLQ_X_SPLIT;
+  static constexpr int SPLIT = 1;
   static constexpr int MMA_WARPS = 2 * SPLIT;
-  // (measured at C3: 16 dequantizing warps with one epilogue warpgroup made
-  // the exact GEMM1 11% slower than 8 + 8; the code supports both)
-  // dequantizing warps: DQ_GROUPS groups of 8 (one warpgroup per weight tile)
-  // that take alternate K steps, so that one group's waits overlap the other's math
-  static constexpr int DQ_GROUPS = FAST ? 1 : LLQ_X_DQG;
-  static constexpr int DQ_WARPS = SS ? 0 : 8 * DQ_GROUPS;
-  static constexpr int EPI_WARPS = FAST ? LLQ_X_EPWF : LLQ_X_EPW;  // token groups of one warpgroup each
+  // dequantizing warps: one warpgroup per weight tile (measured at C3: 16 warps, as
+  // two per row or as two groups taking alternate K steps, gained nothing -- the
+  // exact expansion is limited by its conversion and integer pipes, not latency)
+  static constexpr int DQ_WARPS = SS ? 0 : 8;
+  // token groups of one warpgroup each; the fast mode drains a partial sum every K step,
+  // so it takes four warpgroups (measured: two-launch fast layer 176 -> 134 us)
+  static constexpr int EPI_WARPS = FAST ? 16 : 8;
   static constexpr int FIRST_MMA = 2;  // warp 0 loads weights and scales, warp 1 token tiles
   static constexpr int FIRST_DQ = FIRST_MMA + MMA_WARPS;
   static constexpr int FIRST_EPI = FIRST_DQ + DQ_WARPS;
@@ -649,7 +615,6 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     // ------------------------------------------------------- weight producer
     // per item the fp32 scales of both tiles, per K step both packed weight tiles
     if (lane == 0) {
-      XP_INIT
       int issued = 0, rs = 0;
       uint32_t rph = 0;  // weight ring slot and phase
       bool ok = true;
@@ -666,15 +631,12 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           bulk_load(sdst, P.scale + wrow_of(item, 0) * G, sbytes, &sc_full[sbuf]);
           bulk_load(sdst + ROWS * MAX_G, P.scale + wrow_of(item, 1) * G, sbytes, &sc_full[sbuf]);
         }
-        XP(0);
         const CUtensorMap* tw = item.ph == 0 ? &tm_w0 : &tm_w1;
         const int w0 = static_cast<int>(wrow_of(item, 0)), w1 = static_cast<int>(wrow_of(item, 1));
         int kbeg, kper;
         k_range(item, kbeg, kper);
         for (int kc = kbeg; kc < kbeg + kper; kc += C::W_STEPS) {
-          XP(3);
           if (!mbar_wait(&wfree[rs], rph ^ 1, abort_flag, 0x110 + rs)) { ok = false; break; }
-          XP(1);
           mbar_expect_tx(&wfull[rs], C::W_STAGE_BYTES);
           uint8_t* wdst = sw + rs * C::W_STAGE_BYTES;
           if (C::SS) {  // bf16 rows: two 64-element, 128-byte-swizzled boxes per tile
@@ -686,7 +648,6 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
             tma_load_2d(wdst, tw, kc * C::W_ROW_BYTES, w0, &wfull[rs]);
             tma_load_2d(wdst + C::W_TILE_BYTES, tw, kc * C::W_ROW_BYTES, w1, &wfull[rs]);
           }
-          XP(2);
           ++issued;
           if (++rs == WS) {
             rs = 0;
@@ -694,7 +655,6 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           }
         }
       }
-      XP_SAVE(0);
       // never leave copies in flight into this CTA's shared memory
       for (int i = (issued > WS ? issued - WS : 0); i < issued; ++i) {
         const long long t0 = clock64();
@@ -706,7 +666,6 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     // -------------------------------------------------------- token producer
     // per K step the token tile [rows x 128] bf16, into a slot the step's MMAs released
     if (lane == 0) {
-      XP_INIT
       int issued = 0, rs = 0;
       uint32_t rph = 0;  // token ring slot and phase
       bool ok = true;
@@ -729,7 +688,6 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           if (!ready) break;
           asm volatile("fence.proxy.async.global;" ::: "memory");  // generic stores of h -> TMA reads
         }
-        XP(0);
         const int bi = box_index(item.rows_t);
         const int box = 16 << bi;
         const CUtensorMap* tb =
@@ -738,14 +696,11 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         int kbeg, kper;
         k_range(item, kbeg, kper);
         for (int kc = kbeg; kc < kbeg + kper; ++kc) {
-          XP(3);
           if (!mbar_wait(&mdone[rs], rph ^ 1, abort_flag, 0x118 + rs)) { ok = false; break; }
-          XP(1);
           mbar_expect_tx(&bfull[rs], (C::KS / 64) * box * 128);
           uint8_t* bdst = sb + rs * C::B_STAGE_BYTES;
           tma_load_2d(bdst, tb, kc * C::KS, item.row0, &bfull[rs]);
           if (C::KS == 128) tma_load_2d(bdst + box * 128, tb, kc * C::KS + 64, item.row0, &bfull[rs]);
-          XP(2);
           ++issued;
           if (++rs == BS) {
             rs = 0;
@@ -753,7 +708,6 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           }
         }
       }
-      XP_SAVE(1);
       for (int i = (issued > BS ? issued - BS : 0); i < issued; ++i) {
         const long long t0 = clock64();
         while (!mbar_try_wait(&bfull[i % BS], (i / BS) & 1) && clock64() - t0 < kTimeoutCycles) {
@@ -767,7 +721,6 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     // the whole warp runs the loop (its descriptor arithmetic stays warp-uniform);
     // one elected lane issues the MMAs and the commits that track them
     const uint32_t leader = elect_one();
-    XP_INIT
     {
       const uint32_t a_base = tmem + C::ACC_COLS;
       int it = 0, rs = 0, ra = 0, ws = 0;
@@ -781,10 +734,8 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         if (!FAST) {
           const int ab = C::ACC_BUFS == 2 ? (ii & 1) : 0;
           const uint32_t ph = C::ACC_BUFS == 2 ? ((ii >> 1) & 1) : (ii & 1);
-          XP(4);
           if (!mbar_wait(&acc_empty[ab], ph ^ 1, abort_flag, 0x200)) break;
           tc_fence_after();
-          XP(0);
         }
         int kbeg, kper;
         k_range(item, kbeg, kper);
@@ -795,22 +746,17 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           uint32_t d0 = acc_base + par * NTM, d1 = acc_base + (SPLIT + par) * NTM;
           if (FAST) {
             const int pb = it & 1;
-            XP(4);
             if (!mbar_wait(&acc_empty[pb], ((it >> 1) & 1) ^ 1, abort_flag, 0x210 + pb)) { ok = false; break; }
-            XP(0);
             d0 = tmem + pb * 2 * NTM;
             d1 = d0 + NTM;
           }
-          XP(4);
           if (!mbar_wait(&bfull[s], rph, abort_flag, 0x220 + s)) { ok = false; break; }
-          XP(1);
           if (C::SS) {
             if (!mbar_wait(&wfull[ws], wph, abort_flag, 0x240 + ws)) { ok = false; break; }
           } else if (!mbar_wait(&a_full[tile * AS + sa], raph, abort_flag, 0x230 + sa)) {
             ok = false;
             break;
           }
-          XP(2);
           tc_fence_after();
           // descriptors advance by plain adds on the 16-byte-unit start address
           const uint64_t bdesc0 = make_sdesc(smem_u32(sb + s * C::B_STAGE_BYTES));
@@ -828,7 +774,7 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
               const uint64_t adesc = make_sdesc(smem_u32(sw + ws * C::W_STAGE_BYTES + tile * C::W_TILE_BYTES)) +
                                      (j >> 2) * static_cast<uint64_t>((ROWS * 128) >> 4) + (j & 3) * 2;
               tc_mma_ss(d, adesc, bdesc, idesc, acc, leader);
-            } else if (!LLQ_X_NOMMA) {
+            } else {
               tc_mma(d, a_stage + j * 8, bdesc, idesc, acc, leader);
             }
           }
@@ -841,7 +787,6 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
             }
           }
           if (!FAST && kc == kend - 1) tc_commit(&acc_full[C::ACC_BUFS == 2 ? (ii & 1) : 0], leader);
-          XP(3);
           if (++rs == BS) {
             rs = 0;
             rph ^= 1;
@@ -853,10 +798,8 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         }
       }
     }
-    if (warp == FIRST_MMA) XP_SAVE(2);
   } else if (warp < FIRST_EPI) {
     // ------------------------------------------------------------- dequant
-    const int grp = (warp - FIRST_DQ) >> 3;        // this group takes steps it with it % DQ_GROUPS == grp
     const int wg = ((warp - FIRST_DQ) >> 2) & 1;  // weight tile
     const int q = warp & 3;                 // TMEM lane quarter
     const int r = q * 32 + lane;            // row within the tile
@@ -866,14 +809,11 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     int it = 0, rs = 0, ps = BS - AS, ra = 0;
     uint32_t rph = 0, pph = 1;
     bool ok = true;
-    XP_INIT
     for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
       const Item item = item_at(u);
       const TcPhase& P = args.ph[item.ph];
       const int sbuf = ii & 1;
-      XP(6);
       if (!mbar_wait(&sc_full[sbuf], (ii >> 1) & 1, abort_flag, 0x300)) break;
-      XP(0);
       const float* srow = ssc + sbuf * (2 * ROWS * MAX_G) + wg * (ROWS * MAX_G) + r * P.groups;
       const int spg = P.group / KC;  // K steps per scale group (0: one scale per row)
       int kbeg, kper;
@@ -882,18 +822,9 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         const int s = rs, sa = ra;
         const int half = (kc - kbeg) % C::W_STEPS;  // K step within the weight stage
         const bool stage_done = half == C::W_STEPS - 1 || kc == kbeg + kper - 1;
-        if (C::DQ_GROUPS > 1 && it % C::DQ_GROUPS != grp) {
-          // another group's step: only hand back our share of the weight stage
-          if (stage_done) {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&wfree[s]);
-          }
-        } else {
         const float sc = FAST ? 0.f : srow[spg == 1 ? kc : spg == 0 ? 0 : kc / spg];
         const NibbleScales nsc = nibble_scales(sc);
-        XP(6);
         if (!mbar_wait(&wfull[s], rph, abort_flag, 0x310 + s)) { ok = false; break; }
-        XP(1);
         const uint8_t* wt = sw + s * C::W_STAGE_BYTES + wg * C::W_TILE_BYTES + r * C::W_LOAD_BYTES;
         const uint32_t a_stage = a_row + sa * C::A_STAGE_COLS;
         // this row's packed bytes into registers, then hand the weight slot back
@@ -910,16 +841,13 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (stage_done && lane == 0) mbar_arrive(&wfree[s]);
-        XP(2);
         // the TMEM A stage is free once the MMAs of step it - AS completed
         if (it >= AS && !mbar_wait(&mdone[ps], pph, abort_flag, 0x320 + sa)) { ok = false; break; }
-        XP(3);
         tc_fence_after();
         if (BITS == 4) {
 #pragma unroll
           for (int ci = 0; ci < MYC; ++ci) {
             uint32_t o[16];
-            if (LLQ_X_NODQ) continue;
             if (FAST) codes_int4(v[ci], o);
             else dequant_int4_exact(v[ci], sc, nsc, o);
             tc_st16(a_stage + ci * 16, o);
@@ -933,13 +861,10 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
             tc_st16(a_stage + ci * 8, o);
           }
         }
-        XP(4);
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[wg * AS + sa]);
-        XP(5);
-        }
         if (stage_done && ++rs == WS) {
           rs = 0;
           rph ^= 1;
@@ -954,7 +879,6 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
       __syncwarp();
       if (ok && lane == 0) mbar_arrive(&sc_empty[sbuf]);
     }
-    if (warp == FIRST_DQ) XP_SAVE(3);
   } else {
     // ------------------------------------------------------------- epilogue
     const int eg = (warp - FIRST_EPI) >> 2;  // token half
@@ -965,7 +889,6 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
     constexpr int HALF = NTM / EG;
     int it = 0;
     bool ok = true;
-    XP_INIT
     for (int u = blockIdx.x, ii = 0; u < total_items && ok; u += gridDim.x, ++ii) {
       const Item item = item_at(u);
       const TcPhase& P = args.ph[item.ph];
@@ -1037,10 +960,8 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         const float* s1row = s0row + ROWS * MAX_G;
         for (int kc = 0; kc < P.K / KC; ++kc, ++it) {
           const int pb = it & 1;
-          XP(2);
           if (!mbar_wait(&mdone[it % BS], (it / BS) & 1, abort_flag, 0x410 + pb)) { ok = false; break; }
           tc_fence_after();
-          XP(0);
           const int gi = P.group > 0 ? (kc * KC) / P.group : 0;
           const float s0 = s0row[gi], s1 = s1row[gi];
           const uint32_t p0 = tmem + lane_addr + pb * 2 * NTM + t_begin, p1 = p0 + NTM;
@@ -1062,7 +983,6 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[pb]);
-          XP(1);
         }
         if (!ok) break;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // scale reads before the bulk refill
@@ -1074,10 +994,8 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         const int ab = C::ACC_BUFS == 2 ? (ii & 1) : 0;
         const uint32_t ph = C::ACC_BUFS == 2 ? ((ii >> 1) & 1) : (ii & 1);
         const uint32_t acc_base = tmem + ab * C::ACC_BUF_COLS;
-        XP(2);
         if (!mbar_wait(&acc_full[ab], ph, abort_flag, 0x420)) break;
         tc_fence_after();
-        XP(0);
 #pragma unroll
         for (int c = 0; c < HALF / 16; ++c) {
           const int t0 = t_begin + c * 16;
@@ -1105,7 +1023,6 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[ab]);
-        XP(1);
       }
       if (args.fused && item.ph == 0) {
         // this warp's rows of h are stored: count it for the token tile's GEMM2 items
@@ -1114,7 +1031,6 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
         if (lane == 0) atomicAdd(args.tile_done + item.tg, 1);
       }
     }
-    if (warp == FIRST_EPI) XP_SAVE(4);
   }
 
   if ((!GEMM1 || args.fused) && args.ep_on && warp >= FIRST_EPI) __threadfence_system();  // rows stored to peers
@@ -1464,9 +1380,3 @@ int dense_linear_tc(const void* x, int64_t M, int K, int N, const int8_t* q, con
 }
 
 }  // namespace llq
-
-#if LLQ_X_PROF
-extern "C" int llq_x_prof_read(long long* host) {
-  return cudaMemcpyFromSymbol(host, g_xprof, sizeof(long long) * 256 * 48) == cudaSuccess ? 0 : 3;
-}
-#endif
