@@ -1134,8 +1134,11 @@ int launch_kernel(const CUtensorMap (&tw)[2], const CUtensorMap (&tb)[2][4], con
   if (first_use_on_device(attr))
     cudaFuncSetAttribute(moe_gemm_tc_kernel<GEMM1, BITS, FAST, NTM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(C::SMEM_BYTES));
-  launch_pdl(moe_gemm_tc_kernel<GEMM1, BITS, FAST, NTM>, dim3(num_sms()), dim3(C::THREADS), C::SMEM_BYTES, st,
-             tw[0], tb[0][0], tb[0][1], tb[0][2], tb[0][3], tw[1], tb[1][0], tb[1][1], tb[1][2], tb[1][3], a);
+  // one CTA per SM; a fused launch's GEMM2 items wait for other CTAs' GEMM1 items, so it
+  // is launched cooperatively and fails at launch where its grid cannot be co-resident
+  launch_pdl_ex(a.fused != 0, moe_gemm_tc_kernel<GEMM1, BITS, FAST, NTM>, dim3(num_sms()), dim3(C::THREADS),
+                C::SMEM_BYTES, st, tw[0], tb[0][0], tb[0][1], tb[0][2], tb[0][3], tw[1], tb[1][0], tb[1][1],
+                tb[1][2], tb[1][3], a);
   return check_launch("moe_gemm_tc_kernel");
 }
 
