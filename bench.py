@@ -594,8 +594,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         x = xs[i % N_LAYERS]
         if world > 1:
             return ep.ep_moe_layer(x, gate_w, layer, TOPK, rank, world, bias=bias, impl=impl, window=window)
-        tw, ids, _ = ops._route_impl(x, gate_w, TOPK, bias, False)
-        return ops._fused_moe_packed_impl(x, layer.qw1, layer.sw1, layer.qw2, layer.sw2, tw, ids, BITS, impl)
+        return ops._moe_block_packed_impl(x, gate_w, bias, False, layer.qw1, layer.sw1, layer.qw2, layer.sw2, TOPK,
+                                          BITS, impl)[0]
 
     def barrier():
         if world > 1:
@@ -868,8 +868,8 @@ def measure_c4(args, steps: int, warmup: int) -> dict:
     def step(_i=0):
         x = x0
         for lay in layers:
-            tw, ids, _ = ops._route_impl(x, gate_w, TOPK, None, False)
-            y = ops._fused_moe_packed_impl(x, lay.qw1, lay.sw1, lay.qw2, lay.sw2, tw, ids, BITS, impl)
+            y = ops._moe_block_packed_impl(x, gate_w, None, False, lay.qw1, lay.sw1, lay.qw2, lay.sw2, TOPK, BITS,
+                                           impl)[0]
             x = x + y
         return x
 

@@ -279,6 +279,24 @@ int llq_fused_moe_packed(const void* x, const int8_t* qw1, const float* sw1, con
                          void* stream);
 
 /*
+ * The PACKED MoE block's forward, router included: logits = x . gate_w^T,
+ * softmax(+ bias), top-k, then the routed experts as llq_fused_moe_packed.
+ * It replaces the block forward that runs the router
+ * (trajectory/llada.py:225-234 restates it) and then calls fused_moe
+ * (INFERENCE_REPO_CHANGES.md:109-111), in one call: router, alignment,
+ * permute, expert GEMMs and combine on one stream.  gate_w bf16 [E, H];
+ * bias float32 [E] or NULL; logits bf16 [T, E] or NULL (written when given);
+ * topk_w float32 [T, k] and topk_ids int32 [T, k] are written (the routing the
+ * experts consumed); workspace as for llq_fused_moe_packed (same size).
+ */
+int llq_moe_block_packed(const void* x, const void* gate_w, const float* bias, int renormalize,
+                         int64_t T, int E, int H, int I, int k, const int8_t* qw1,
+                         const float* sw1, const int8_t* qw2, const float* sw2, int bits,
+                         int group_size, void* logits, float* topk_w, int32_t* topk_ids,
+                         void* out, void* workspace, size_t workspace_bytes, int impl,
+                         void* stream);
+
+/*
  * No counterpart in the reference.  The same layer as llq_fused_moe_packed for
  * callers that cannot allocate device memory (a plugin inside a framework that
  * owns the allocator, a runtime that reserves all memory at start-up): no

@@ -49,6 +49,7 @@ SIGNATURES = {
     "llq_moe_workspace_size": (c_size_t, [L, I, I, I, I]),
     "llq_fused_moe_packed": (I, [P, P, P, P, P, P, P, L, I, I, I, I, I, I, P, P, c_size_t, I, P]),
     "llq_fused_moe_packed_noalloc": (I, [P, P, P, P, P, P, P, L, I, I, I, I, I, I, P, I, P]),
+    "llq_moe_block_packed": (I, [P, P, P, I, L, I, I, I, I, P, P, P, P, I, I, P, P, P, P, P, c_size_t, I, P]),
     "llq_ep_window_bytes": (c_size_t, [I, I, I]),
     "llq_ep_set_timeout_ms": (I, [I]),
     "llq_ipc_handle_bytes": (I, []),

@@ -234,28 +234,18 @@ size_t llq_moe_workspace_size(int64_t T, int k, int E, int H, int I) {
   return carve(nullptr, T, k, E, H, I).total;
 }
 
-int llq_fused_moe_packed(const void* x, const int8_t* qw1, const float* sw1, const int8_t* qw2,
-                         const float* sw2, const float* topk_w, const int32_t* topk_ids, int64_t T,
-                         int E, int H, int I, int k, int bits, int group_size, void* out,
-                         void* workspace, size_t workspace_bytes, int impl, void* stream) {
-  if (T < 0 || E < 1 || H < 1 || I < 1 || k < 1 || k > E)
-    return fail(LLQ_EINVAL, "bad shape T=%lld E=%d H=%d I=%d k=%d", (long long)T, E, H, I, k);
-  if (T == 0) return LLQ_OK;
-  MoeWorkspace ws = carve(workspace, T, k, E, H, I);
-  if (workspace == nullptr || workspace_bytes < ws.total)
-    return fail(LLQ_ENOSPACE, "workspace needs %zu bytes, got %zu", ws.total, workspace_bytes);
-  cudaStream_t st = as_stream(stream);
+}  // extern "C"
+
+namespace llq {
+namespace {
+
+// the layer after the alignment: permute, expert GEMMs, combine
+int experts_after_align(const MoeWorkspace& ws, const void* x, const int8_t* qw1, const float* sw1,
+                        const int8_t* qw2, const float* sw2, const float* topk_w, int64_t T, int E, int H, int I,
+                        int k, int bits, int group_size, void* out, int impl, cudaStream_t st) {
   const int64_t n = T * k;
-  AlignMask am{};
-  am.clear = ws.tile_done;
-  am.clear_n = ws.tile_done_n;
-  int rc = align_impl_masked(topk_ids, n, E, ws.offsets, ws.sorted_slots, ws.align_ws, ws.align_bytes, st, am);
-  if (rc) return rc;
+  int rc;
   if (impl == LLQ_GEMM_TCGEN05_FAST) {
-    if (pick_impl(impl, E, I, H, bits, group_size, true) < 0 ||
-        pick_impl(impl, E, H, I, bits, group_size, false) < 0)
-      return fail(LLQ_EUNSUPPORTED, "LLQ_GEMM_TCGEN05_FAST does not cover this shape (INT4, K <= 2048, "
-                                    "I %% 128 == 0, H %% 256 == 0, group %% 128 == 0)");
     rc = permute_impl(x, T, H, k, ws.sorted_slots, ws.x_sorted, st, 1);
     if (rc) return rc;
     rc = gemm12_fused_tc(ws.x_sorted, ws.offsets, ws.sorted_slots, topk_w, n, E, H, I, qw1, sw1, qw2, sw2, bits,
@@ -286,13 +276,74 @@ int llq_fused_moe_packed(const void* x, const int8_t* qw1, const float* sw1, con
     if (rc) return rc;
     return combine_impl(ws.y_slots, T, k, H, out, st);
   }
-  rc = llq_moe_gemm1(ws.x_sorted, ws.offsets, n, E, H, I, qw1, sw1, bits, group_size, ws.h_sorted,
-                     impl, stream);
+  void* stream = st;
+  rc = llq_moe_gemm1(ws.x_sorted, ws.offsets, n, E, H, I, qw1, sw1, bits, group_size, ws.h_sorted, impl, stream);
   if (rc) return rc;
-  rc = llq_moe_gemm2(ws.h_sorted, ws.offsets, ws.sorted_slots, topk_w, n, E, H, I, qw2, sw2, bits,
-                     group_size, ws.y_slots, impl, stream);
+  rc = llq_moe_gemm2(ws.h_sorted, ws.offsets, ws.sorted_slots, topk_w, n, E, H, I, qw2, sw2, bits, group_size,
+                     ws.y_slots, impl, stream);
   if (rc) return rc;
   return combine_impl(ws.y_slots, T, k, H, out, st);
+}
+
+int check_fast(int impl, int E, int H, int I, int bits, int group_size) {
+  if (impl == LLQ_GEMM_TCGEN05_FAST && (pick_impl(impl, E, I, H, bits, group_size, true) < 0 ||
+                                        pick_impl(impl, E, H, I, bits, group_size, false) < 0))
+    return fail(LLQ_EUNSUPPORTED, "LLQ_GEMM_TCGEN05_FAST does not cover this shape (INT4, K <= 2048, "
+                                  "I %% 128 == 0, H %% 256 == 0, group %% 128 == 0)");
+  return LLQ_OK;
+}
+
+// the alignment of a layer call: offsets and sorted slots; zeroes the GEMM tile counters
+int align_layer(const MoeWorkspace& ws, const int32_t* topk_ids, int64_t n, int E, cudaStream_t st) {
+  AlignMask am{};
+  am.clear = ws.tile_done;
+  am.clear_n = ws.tile_done_n;
+  return align_impl_masked(topk_ids, n, E, ws.offsets, ws.sorted_slots, ws.align_ws, ws.align_bytes, st, am);
+}
+
+}  // namespace
+}  // namespace llq
+
+extern "C" {
+
+int llq_fused_moe_packed(const void* x, const int8_t* qw1, const float* sw1, const int8_t* qw2,
+                         const float* sw2, const float* topk_w, const int32_t* topk_ids, int64_t T,
+                         int E, int H, int I, int k, int bits, int group_size, void* out,
+                         void* workspace, size_t workspace_bytes, int impl, void* stream) {
+  if (T < 0 || E < 1 || H < 1 || I < 1 || k < 1 || k > E)
+    return fail(LLQ_EINVAL, "bad shape T=%lld E=%d H=%d I=%d k=%d", (long long)T, E, H, I, k);
+  if (T == 0) return LLQ_OK;
+  MoeWorkspace ws = carve(workspace, T, k, E, H, I);
+  if (workspace == nullptr || workspace_bytes < ws.total)
+    return fail(LLQ_ENOSPACE, "workspace needs %zu bytes, got %zu", ws.total, workspace_bytes);
+  int rc = check_fast(impl, E, H, I, bits, group_size);
+  if (rc) return rc;
+  cudaStream_t st = as_stream(stream);
+  rc = align_layer(ws, topk_ids, T * k, E, st);
+  if (rc) return rc;
+  return experts_after_align(ws, x, qw1, sw1, qw2, sw2, topk_w, T, E, H, I, k, bits, group_size, out, impl, st);
+}
+
+int llq_moe_block_packed(const void* x, const void* gate_w, const float* bias, int renormalize, int64_t T, int E,
+                         int H, int I, int k, const int8_t* qw1, const float* sw1, const int8_t* qw2,
+                         const float* sw2, int bits, int group_size, void* logits, float* topk_w,
+                         int32_t* topk_ids, void* out, void* workspace, size_t workspace_bytes, int impl,
+                         void* stream) {
+  if (T < 0 || E < 1 || H < 1 || I < 1 || k < 1 || k > E)
+    return fail(LLQ_EINVAL, "bad shape T=%lld E=%d H=%d I=%d k=%d", (long long)T, E, H, I, k);
+  if (T == 0) return LLQ_OK;
+  if (topk_w == nullptr || topk_ids == nullptr) return fail(LLQ_EINVAL, "null topk_w / topk_ids");
+  MoeWorkspace ws = carve(workspace, T, k, E, H, I);
+  if (workspace == nullptr || workspace_bytes < ws.total)
+    return fail(LLQ_ENOSPACE, "workspace needs %zu bytes, got %zu", ws.total, workspace_bytes);
+  int rc = check_fast(impl, E, H, I, bits, group_size);
+  if (rc) return rc;
+  cudaStream_t st = as_stream(stream);
+  rc = route_impl(x, gate_w, T, H, E, k, bias, renormalize, logits, topk_w, topk_ids, st);
+  if (rc) return rc;
+  rc = align_layer(ws, topk_ids, T * k, E, st);
+  if (rc) return rc;
+  return experts_after_align(ws, x, qw1, sw1, qw2, sw2, topk_w, T, E, H, I, k, bits, group_size, out, impl, st);
 }
 
 int llq_device_error(int32_t* code) {

@@ -21,11 +21,11 @@ namespace {
 constexpr int kMaxExperts = 256;
 
 // softmax + top-k of one token held by one warp: value j of the lane is
-// expert lane + 32 j
+// expert lane + 32 j (J values per lane: E <= 32 J)
+template <int J = kMaxExperts / 32>
 __device__ void warp_softmax_topk(float (&v)[kMaxExperts / 32], int E, int k, int renormalize,
                                   float* __restrict__ topk_w, int32_t* __restrict__ topk_ids) {
   const int lane = threadIdx.x & 31;
-  constexpr int J = kMaxExperts / 32;
   float m = -__int_as_float(0x7f800000);
 #pragma unroll
   for (int j = 0; j < J; ++j)
@@ -48,26 +48,23 @@ __device__ void warp_softmax_topk(float (&v)[kMaxExperts / 32], int E, int k, in
   float chosen_w = 0.f;
   int chosen_id = 0;
   for (int r = 0; r < k; ++r) {
-    // lane-local best, then warp argmax with (value desc, id asc)
-    float bv = -2.f;
+    // (value desc, id asc): the probabilities are >= +0 and the taken ones -2, so
+    // their bit patterns order like the values as signed integers; one warp max
+    // of the bits, then the smallest id holding it
+    int bb = static_cast<int>(0x80000000u);
     int bi = 0x7fffffff;
 #pragma unroll
     for (int j = 0; j < J; ++j) {
       const int id = lane + 32 * j;
-      if (id < E && (v[j] > bv || (v[j] == bv && id < bi))) {
-        bv = v[j];
+      const int b = __float_as_int(v[j]);
+      if (id < E && b > bb) {  // ids ascend with j: the first of equal values is kept
+        bb = b;
         bi = id;
       }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
+    const int wb = __reduce_max_sync(0xffffffffu, bb);
+    bi = __reduce_min_sync(0xffffffffu, bb == wb ? bi : 0x7fffffff);
+    const float bv = __int_as_float(wb);
     // remove the winner
 #pragma unroll
     for (int j = 0; j < J; ++j)
@@ -286,7 +283,7 @@ __global__ void __launch_bounds__(kRmWarps * 32) route_mma_kernel(const __nv_bfl
       }
       v[j] = l;
     }
-    warp_softmax_topk(v, E, k, renormalize, topk_w + t * k, topk_ids + t * k);
+    warp_softmax_topk<(E + 31) / 32>(v, E, k, renormalize, topk_w + t * k, topk_ids + t * k);
   }
 }
 

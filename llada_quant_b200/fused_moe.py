@@ -81,12 +81,12 @@ def moe_layer(x: torch.Tensor, gate_w: torch.Tensor, packed: PackedExperts, top_
     the device, from the expert offsets the GEMMs used; with a
     ``router_capture.RouterCapture`` the router kernel's own ids and logits are
     recorded under ``name``."""
-    # eager hot path: the op implementations directly (no per-call dispatcher cost)
-    topk_w, topk_ids, logits = ops._route_impl(x, gate_w, top_k, bias, renormalize)
+    # eager hot path: one library call (router through combine), no per-call dispatcher cost
+    out, topk_w, topk_ids, logits = ops._moe_block_packed_impl(
+        x, gate_w, bias, renormalize, packed.qw1, packed.sw1, packed.qw2, packed.sw2, top_k, packed.bits,
+        IMPL[impl], want_logits=capture is not None)
     if capture is not None:
         capture.record(name, topk_ids, logits)
-    out = ops._fused_moe_packed_impl(x, packed.qw1, packed.sw1, packed.qw2, packed.sw2, topk_w,
-                                     topk_ids, packed.bits, IMPL[impl])
     if recorder is not None:
         E = packed.num_experts
         T = x.shape[0]

@@ -479,10 +479,7 @@ def _fused_moe_packed_impl(x: torch.Tensor, qw1: torch.Tensor, sw1: torch.Tensor
     ws = moe_workspace(T, k, E, H, inter, x.device)
     # one config group size; the library applies the per-row fallback to the
     # tensor whose K it does not divide, as quantize_tensor did
-    g1, g2 = _group_of(qw1, sw1, bits), _group_of(qw2, sw2, bits)
-    if g1 != -1 and g2 != -1 and g1 != g2:
-        raise ValueError("w1 and w2 must share the group size")
-    g = g1 if g1 != -1 else g2
+    g = _group_pair(qw1, sw1, qw2, sw2, bits)
     check(load().llq_fused_moe_packed(x.data_ptr(), qw1.data_ptr(), sw1.data_ptr(), qw2.data_ptr(),
                                       sw2.data_ptr(), tw.data_ptr(), ids.data_ptr(), T, E, H, inter,
                                       k, bits, g, out.data_ptr(), ws.data_ptr(), ws.numel(), impl,
@@ -496,6 +493,38 @@ fused_moe_packed = torch.library.custom_op("llada_quant::fused_moe_packed", muta
 @fused_moe_packed.register_fake
 def _(x, qw1, sw1, qw2, sw2, topk_w, topk_ids, bits, impl):
     return torch.empty_like(x, dtype=torch.bfloat16)
+
+
+def _group_pair(qw1: torch.Tensor, sw1: torch.Tensor, qw2: torch.Tensor, sw2: torch.Tensor, bits: int) -> int:
+    g1, g2 = _group_of(qw1, sw1, bits), _group_of(qw2, sw2, bits)
+    if g1 != -1 and g2 != -1 and g1 != g2:
+        raise ValueError("w1 and w2 must share the group size")
+    return g1 if g1 != -1 else g2
+
+
+def _moe_block_packed_impl(x: torch.Tensor, gate_w: torch.Tensor, bias: Optional[torch.Tensor], renormalize: bool,
+                           qw1: torch.Tensor, sw1: torch.Tensor, qw2: torch.Tensor, sw2: torch.Tensor, k: int,
+                           bits: int, impl: int, want_logits: bool = False):
+    """Router + routed experts on PACKED weights in one library call ->
+    (out bf16 [T,H], topk_w f32 [T,k], topk_ids i32 [T,k], logits bf16 [T,E] or None)."""
+    _need_cuda(x, gate_w, bias, qw1, sw1, qw2, sw2)
+    x = x.contiguous()
+    gate_w = gate_w.contiguous()
+    T, H = x.shape
+    E, two_i = qw1.shape[0], qw1.shape[1]
+    inter = two_i // 2
+    tw = torch.empty(T, k, dtype=torch.float32, device=x.device)
+    ids = torch.empty(T, k, dtype=torch.int32, device=x.device)
+    logits = torch.empty(T, E, dtype=torch.bfloat16, device=x.device) if want_logits else None
+    b = None if bias is None else bias.contiguous().to(torch.float32)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
+    ws = moe_workspace(T, k, E, H, inter, x.device)
+    check(load().llq_moe_block_packed(x.data_ptr(), gate_w.data_ptr(), _ptr(b), int(renormalize), T, E, H, inter, k,
+                                      qw1.data_ptr(), sw1.data_ptr(), qw2.data_ptr(), sw2.data_ptr(), bits,
+                                      _group_pair(qw1, sw1, qw2, sw2, bits), _ptr(logits), tw.data_ptr(),
+                                      ids.data_ptr(), out.data_ptr(), ws.data_ptr(), ws.numel(), impl, _stream(x)),
+          "moe_block_packed")
+    return out, tw, ids, logits
 
 
 def device_error() -> int:

@@ -170,3 +170,40 @@ def test_router_capture_records_the_kernels_routing():
     assert "after" not in cap.layer_names
     cap.clear()
     assert cap.layer_names == []
+
+
+@pytest.mark.parametrize("T,H,E,k,bias,renorm", [
+    (256, 2048, 64, 8, False, False),
+    (1, 2048, 64, 8, False, False),
+    (37, 512, 16, 2, True, True),      # ragged token tile, bias, renormalized weights
+    (40, 384, 24, 4, False, False),    # outside the tcgen05 shapes: the CUDA-core GEMMs
+])
+def test_block_call_matches_router_then_layer(T, H, E, k, bias, renorm):
+    """llq_moe_block_packed (router inside the call) against llq_route followed by
+    llq_fused_moe_packed on the same inputs: identical logits, routing and output
+    over repeated calls."""
+    from llada_quant_b200 import ops
+    from llada_quant_b200 import symmetric as G
+    from llada_quant_b200.moe import PackedExperts
+    dev = torch.device("cuda")
+    I = 256
+    g = torch.Generator().manual_seed(T + H + E)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(dev)
+    gw = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+    b = (torch.randn(E, generator=g) * 0.1).to(dev) if bias else None
+    r1 = G.quantize_tensor((torch.randn(E, 2 * I, H, generator=g) * 0.02).to(torch.bfloat16).to(dev), bits=4,
+                           group_size=128)
+    r2 = G.quantize_tensor((torch.randn(E, H, I, generator=g) * 0.02).to(torch.bfloat16).to(dev), bits=4,
+                           group_size=128)
+    p = PackedExperts(r1.q, r1.scale, r2.q, r2.scale, 4, 128)
+    tw, ids, logits = ops.route(x, gw, k, b, renorm)
+    ref = ops.fused_moe_packed(x, p.qw1, p.sw1, p.qw2, p.sw2, tw, ids, 4, 0)
+    for _ in range(3):
+        out, tw2, ids2, lg2 = ops._moe_block_packed_impl(x, gw, b, renorm, p.qw1, p.sw1, p.qw2, p.sw2, k, 4, 0,
+                                                         want_logits=True)
+        torch.cuda.synchronize()
+        assert torch.equal(lg2, logits)
+        assert torch.equal(ids2, ids)
+        assert torch.equal(tw2, tw)
+        assert torch.equal(out, ref)
+    assert ops.device_error() == 0
