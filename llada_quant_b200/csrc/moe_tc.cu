@@ -1016,8 +1016,35 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
             } else {
               tc_wait_ld();
             }
+            if (NTM >= 128 && g1 && args.ksplit <= 1) {
+              // GEMM1 of 128-token tiles: silu(gate) * up for 16 tokens as straight-line
+              // code (the exp of all 16 first, then the divisions, then the stores) so
+              // that the chains overlap (measured with 8 experts x 256 rows: fused launch
+              // 82 -> 72 us; the 64-token tiles, whose epilogue overlaps the next item's
+              // MMAs, keep the per-token form: 117 vs 119 us at C3)
+              float e[16], o[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) emit(c * 16 + i, v0[i], v1[i]);
+              for (int i = 0; i < 16; ++i) {
+                v0[i] = round_bf16(v0[i]);
+                e[i] = __fadd_rn(1.f, expf(-v0[i]));
+              }
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                o[i] = __fmul_rn(round_bf16(__fdiv_rn(v0[i], e[i])), round_bf16(v1[i]));
+              const TcPhase& P1 = args.ph[item.ph];
+              const int n = item.rb * ROWS + r;
+              __nv_bfloat16* col = P1.out + (FAST ? kperm_pos(n) : n);
+              const int tl0 = t_begin + c * 16;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const int t = tl0 + i;
+                if (t < t_end && t < item.rows_t)
+                  col[(static_cast<int64_t>(item.row0) + t) * P1.n_out] = __float2bfloat16_rn(o[i]);
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) emit(c * 16 + i, v0[i], v1[i]);
+            }
           }
         }
         tc_fence_before();
