@@ -449,6 +449,19 @@ __device__ __forceinline__ int kperm_pos(int n) {
   return (n & ~7) | (j < 4 ? 2 * j : 2 * (j - 4) + 1);
 }
 
+// SiLU's quotient g / d (d = 1 + exp(-g) >= 1) as the bf16 value of its correctly
+// rounded fp32 form, without the IEEE division in the common case: the quotient
+// from the approximate reciprocal lies within 2 ulp of g / d, so it rounds to the
+// same bf16 value unless it lies within 8 ulp of a bf16 rounding midpoint (low 16
+// bits 0x8000); those, and d beyond 2^120 or not finite, are flagged in `need`
+// for __fdiv_rn.
+__device__ __forceinline__ float silu_quot_fast(float g, float d, bool& need) {
+  const float q = __fdividef(g, d);
+  const uint32_t lo = __float_as_uint(q) & 0xFFFFu;
+  need = (lo - 0x7FF8u) <= 16u || !(d < 0x1p120f);
+  return q;
+}
+
 __device__ __forceinline__ int box_index(int rows) {
   return rows <= 16 ? 0 : rows <= 32 ? 1 : rows <= 64 ? 2 : 3;
 }
@@ -1028,9 +1041,20 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
                 v0[i] = round_bf16(v0[i]);
                 e[i] = __fadd_rn(1.f, expf(-v0[i]));
               }
+              uint32_t slow = 0;
 #pragma unroll
-              for (int i = 0; i < 16; ++i)
-                o[i] = __fmul_rn(round_bf16(__fdiv_rn(v0[i], e[i])), round_bf16(v1[i]));
+              for (int i = 0; i < 16; ++i) {
+                bool need;
+                o[i] = silu_quot_fast(v0[i], e[i], need);
+                slow |= static_cast<uint32_t>(need) << i;
+              }
+              if (slow != 0) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                  if ((slow >> i) & 1u) o[i] = __fdiv_rn(v0[i], e[i]);
+              }
+#pragma unroll
+              for (int i = 0; i < 16; ++i) o[i] = __fmul_rn(round_bf16(o[i]), round_bf16(v1[i]));
               const TcPhase& P1 = args.ph[item.ph];
               const int n = item.rb * ROWS + r;
               __nv_bfloat16* col = P1.out + (FAST ? kperm_pos(n) : n);
