@@ -61,7 +61,21 @@ __global__ void __launch_bounds__(kDispatchThreads) ep_dispatch_kernel(
     const int64_t at = static_cast<int64_t>(me) * L.cap + pos;
     const uint4* src = x + (i / k) * vpr;
     uint4* dst = reinterpret_cast<uint4*>(peer + L.rows) + at * vpr;
-    for (int v = lane; v < vpr; v += 32) dst[v] = __ldg(src + v);
+    // all of a lane's loads of a 4 KiB slice before its stores: one round trip per slice
+    constexpr int U = 8;
+    for (int v0 = 0; v0 < vpr; v0 += 32 * U) {
+      uint4 buf[U];
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        const int v = v0 + j * 32 + lane;
+        if (v < vpr) buf[j] = __ldg(src + v);
+      }
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        const int v = v0 + j * 32 + lane;
+        if (v < vpr) dst[v] = buf[j];
+      }
+    }
     if (lane == 0) {
       reinterpret_cast<int32_t*>(peer + L.ids)[at] = e - d * experts_per_rank;
       reinterpret_cast<float*>(peer + L.wts)[at] = topk_w[i];
