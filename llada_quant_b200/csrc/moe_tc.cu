@@ -1048,11 +1048,6 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
                 o[i] = silu_quot_fast(v0[i], e[i], need);
                 slow |= static_cast<uint32_t>(need) << i;
               }
-              if (slow != 0) {
-#pragma unroll
-                for (int i = 0; i < 16; ++i)
-                  if ((slow >> i) & 1u) o[i] = __fdiv_rn(v0[i], e[i]);
-              }
 #pragma unroll
               for (int i = 0; i < 16; ++i) o[i] = __fmul_rn(round_bf16(o[i]), round_bf16(v1[i]));
               const TcPhase& P1 = args.ph[item.ph];
@@ -1064,6 +1059,27 @@ __global__ void __launch_bounds__((Cfg<GEMM1, BITS, FAST, NTM>::THREADS), 1)
                 const int t = tl0 + i;
                 if (t < t_end && t < item.rows_t)
                   col[(static_cast<int64_t>(item.row0) + t) * P1.n_out] = __float2bfloat16_rn(o[i]);
+              }
+              // rare (quotients near a bf16 rounding midpoint): those tokens again from the
+              // accumulators, still in TMEM, with the IEEE division, stored over the fast
+              // values.  Kept after the stores so that the common path holds no extra
+              // values live (a fallback inside it made the launch 9 us slower).
+              if (__any_sync(0xffffffffu, slow != 0)) {
+                static_assert(SPLIT == 1, "the fallback reloads one accumulator per tile");
+                float w0[16], w1[16];
+                tc_ld16(acc_base + lane_addr + t0, w0);
+                tc_ld16(acc_base + lane_addr + SPLIT * NTM + t0, w1);
+                tc_wait_ld();
+#pragma unroll 1
+                for (int i = 0; i < 16; ++i) {
+                  const int t = tl0 + i;
+                  if (((slow >> i) & 1u) && t < t_end && t < item.rows_t) {
+                    const float g = round_bf16(w0[i]);
+                    const float q = __fdiv_rn(g, __fadd_rn(1.f, expf(-g)));
+                    col[(static_cast<int64_t>(item.row0) + t) * P1.n_out] =
+                        __float2bfloat16_rn(__fmul_rn(round_bf16(q), round_bf16(w1[i])));
+                  }
+                }
               }
             } else {
 #pragma unroll
