@@ -90,8 +90,10 @@ struct Cfg {
   // exact expansion is limited by its conversion and integer pipes, not latency)
   static constexpr int DQ_WARPS = SS ? 0 : 8;
   // token groups of one warpgroup each; the fast mode drains a partial sum every K step,
-  // so it takes four warpgroups (measured: two-launch fast layer 176 -> 134 us)
-  static constexpr int EPI_WARPS = FAST ? 16 : 8;
+  // so it takes four warpgroups (measured: two-launch fast layer 176 -> 134 us), and so
+  // does the bf16 prefill kernel, which has no dequantizing warps and whose epilogues
+  // of 128-token tiles set its pace (measured: C4 step 95.2 -> 73.0 ms)
+  static constexpr int EPI_WARPS = (FAST || SS) ? 16 : 8;
   static constexpr int FIRST_MMA = 2;  // warp 0 loads weights and scales, warp 1 token tiles
   static constexpr int FIRST_DQ = FIRST_MMA + MMA_WARPS;
   static constexpr int FIRST_EPI = FIRST_DQ + DQ_WARPS;
