@@ -57,6 +57,13 @@ def test_argument_validation_needs_no_gpu():
     assert rc == _lib.LLQ_EINVAL and b"max_shrink" in lib.llq_last_error()
     rc = lib.llq_fused_moe_packed(*([None] * 7), 4, 8, 64, 32, 2, 4, 128, None, None, 0, 0, None)
     assert rc == _lib.LLQ_ENOSPACE
+    # the block call: bad shape, missing routing outputs, no workspace -- all before any launch
+    blk = lambda T, E, k, tw, ids: lib.llq_moe_block_packed(None, None, None, 0, T, E, 64, 32, k, None, None, None,
+                                                             None, 4, 128, None, tw, ids, None, None, 0, 0, None)
+    assert blk(4, 8, 9, 1, 1) == _lib.LLQ_EINVAL and b"bad shape" in lib.llq_last_error()
+    assert blk(4, 8, 2, None, 1) == _lib.LLQ_EINVAL and b"topk_w" in lib.llq_last_error()
+    assert blk(4, 8, 2, 1, 1) == _lib.LLQ_ENOSPACE
+    assert blk(0, 8, 2, None, None) == _lib.LLQ_OK
 
 
 def _a256(v):
